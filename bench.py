@@ -1,0 +1,467 @@
+#!/usr/bin/env python
+"""Benchmark of the k200 matmul hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...   (N > 1)
+
+Workload (the metric's configuration): the Q4_0 GEMVs of a
+7B MLP at batch 1, chained as up then down:
+    y1[1,11008] = x[1,4096]   . W_up^T   (K=4096,  N=11008)
+    y2[1,4096]  = y1[1,11008] . W_down^T (K=11008, N=4096)
+One step = both GEMVs over one activation vector.  Weights are Q4_0 blocks of
+N(0, 0.02) values (GGML quantiser on the device), X is U[-1, 1] (synthetic,
+seeded).  With N GPUs each weight is row-sharded N ways and each output is
+all-gathered over NCCL, so the down projection sees the full y1.
+
+Metric: Q4_0 weight GB/s (weight bytes of both matrices per step / step time,
+whole job), the HBM-bound figure of merit the reference reports for its Q4
+GEMV.  Between timed steps the weights rotate through enough distinct sets
+that the whole rotation exceeds twice the L2 size, so every step streams its
+weights from HBM.
+
+--impl reference times the reference's CPU implementation of the same path
+(bench/native-q4-reference.h reference(), compiled from the reference sources
+into oracle/_ref; the C restatement in oracle/ when that is absent) on the
+host cores, one bounded sample of the workload per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+UP = (4096, 11008)    # (K, N)
+DOWN = (11008, 4096)
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def q4_bytes(k: int, n: int) -> int:
+    return n * (k // 32) * 18
+
+
+def read_peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": FALLBACK_HBM_GBS, "source": "fallback"}
+
+
+def profile_traffic(name: str):
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", name)
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(float(line.split(":", 1)[1].strip()))
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms during a window."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.file = None
+        self.t0 = self.t1 = None
+
+    def start(self):
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.device)], stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def mark(self, begin: bool):
+        if begin:
+            self.t0 = time.time()
+        else:
+            self.t1 = time.time()
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        rows = []
+        with open(self.file.name) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+                except ValueError:
+                    continue
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# CPU arm (reference implementation on the host cores)
+# ---------------------------------------------------------------------------
+def cpu_weights(seed: int, k: int, n: int):
+    import oracle as O
+
+    w = O.normal(seed, n * k, 0.0, 0.02)
+    q4 = O.q4_0_quantize(w, n, k)
+    return q4, O.q4_0_dequantize(q4, n, k)
+
+
+def cpu_step_fn(threads: int):
+    """One (possibly row-sampled) up+down step of the reference CPU GEMV."""
+    import oracle as O
+
+    R = O.ref()
+    kind = "reference" if R is not None else "port"
+    dec_up = cpu_weights(11, *UP)[1]
+    dec_down = cpu_weights(12, *DOWN)[1]
+    x = O.uniform(0x09200ABC, UP[0], -1.0, 1.0)
+    handles = {}
+
+    def prepared(idx, dec, k, rows):
+        key = (idx, rows)
+        if key not in handles:
+            handles[key] = R.ref_gemv_create(np.ascontiguousarray(dec[: rows * k]), k, rows, threads)
+        return handles[key]
+
+    def step(frac: float) -> int:
+        """Runs both GEMVs over the first `frac` of their rows; returns Q4 bytes covered."""
+        covered = 0
+        inp = x
+        for idx, ((k, n), dec) in enumerate(((UP, dec_up), (DOWN, dec_down))):
+            rows = max(1, int(round(n * frac)))
+            y = np.empty(rows, np.float64)
+            xin = np.ascontiguousarray(inp[:k], np.float32)
+            if R is not None:
+                R.ref_gemv_run(prepared(idx, dec, k, rows), xin, 1, y)
+            else:
+                O.lib().ko_reference_fp64(dec[: rows * k], xin, k, rows, 1, y, threads)
+            covered += q4_bytes(k, rows)
+            nxt = np.zeros(n, np.float32)
+            nxt[:rows] = y
+            inp = nxt
+        return covered
+
+    return step, kind
+
+
+def cpu_baseline(seconds: float = 10.0) -> dict:
+    threads = os.cpu_count() or 1
+    step, kind = cpu_step_fn(threads)
+    step(0.05)  # warm caches and threads
+    t0 = time.perf_counter()
+    done = nbytes = 0
+    while True:
+        nbytes += step(1.0)
+        done += 1
+        if time.perf_counter() - t0 >= seconds and done >= 2:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": nbytes / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": kind,
+            "sample": f"{done} full up+down Q4_0 GEMV steps (K4096xN11008, K11008xN4096, batch 1), "
+                      f"FP64 reference() over pre-decoded weights, {dt:.1f} s"}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    step, kind = cpu_step_fn(threads)
+    # size one step so that warmup + steps finish in about two minutes
+    t = time.perf_counter()
+    full = step(1.0)
+    t_full = time.perf_counter() - t
+    budget = 120.0 / max(1, args.steps + args.warmup)
+    frac = min(1.0, budget / max(t_full, 1e-6))
+    for _ in range(args.warmup):
+        step(frac)
+    t0 = time.perf_counter()
+    nbytes = 0
+    for _ in range(args.steps):
+        nbytes += step(frac)
+    dt = time.perf_counter() - t0
+    value = nbytes / dt / 1e9
+    sample = (f"each step: the first {frac:.4f} of the rows of both GEMVs "
+              f"({full * frac / 1e6:.2f} MB of Q4_0 weights), FP64 reference() over pre-decoded weights")
+    line = {
+        "impl": "reference", "metric": "q4_0_gemv_weight_gbps", "value": value, "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt / max(1, args.steps) * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": "q4_0 GEMV 7B MLP up+down, batch 1 (config 1)", "up": "K4096xN11008",
+                   "down": "K11008xN4096"},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    import kunlunk200_lib_b200 as K
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dev = local
+    K.select(dev)
+    stream = torch.cuda.Stream()
+    K.set_stream(dev, stream.cuda_stream)
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+
+    for k, n in (UP, DOWN):
+        if n % world:
+            raise SystemExit(f"N={n} does not split over {world} GPUs")
+    n_up, n_down = UP[1] // world, DOWN[1] // world
+    shard_bytes = q4_bytes(UP[0], n_up) + q4_bytes(DOWN[0], n_down)
+    total_bytes = q4_bytes(*UP) + q4_bytes(*DOWN)
+    sets = max(2, math.ceil(2 * l2 / shard_bytes) + 1)
+
+    gen = torch.Generator(device="cuda")
+    weights = []
+    with torch.cuda.stream(stream):
+        for s in range(sets):
+            pair = []
+            for m, (k, n) in enumerate(((UP[0], n_up), (DOWN[0], n_down))):
+                gen.manual_seed(1000003 * s + 7919 * m + 104729 * rank + 1)
+                w = torch.randn((n, k), generator=gen, device="cuda", dtype=torch.float32) * 0.02
+                q = torch.empty(q4_bytes(k, n), dtype=torch.uint8, device="cuda")
+                K.quantize_q4_0(dev, q, w, k, n)
+                pair.append(q)
+                del w
+            weights.append(pair)
+        gen.manual_seed(0x09200ABC)
+        x = torch.rand(UP[0], generator=gen, device="cuda") * 2 - 1
+        y1_full = torch.empty(UP[1], device="cuda")
+        y2_full = torch.empty(DOWN[1], device="cuda")
+        y1_shard = y1_full if world == 1 else torch.empty(n_up, device="cuda")
+        y2_shard = y2_full if world == 1 else torch.empty(n_down, device="cuda")
+    stream.synchronize()
+    kern = K.Kernel()
+
+    def step(s: int, xin=None):
+        wu, wd = weights[s % sets]
+        K.matmul(kern, dev, y1_shard, wu, x if xin is None else xin, UP[0], n_up, 1, K.Q4_0)
+        if world > 1:
+            dist.all_gather_into_tensor(y1_full, y1_shard)
+        K.matmul(kern, dev, y2_shard, wd, y1_full, DOWN[0], n_down, 1, K.Q4_0)
+        if world > 1:
+            dist.all_gather_into_tensor(y2_full, y2_shard)
+
+    with torch.cuda.stream(stream):
+        for i in range(max(3, args.warmup)):
+            step(i)
+    stream.synchronize()
+    K.check(K.wait())
+
+    # one CUDA graph holds a whole number of rotations; the timed region
+    # replays it until exactly `steps` steps ran (a remainder graph if needed)
+    per_graph = sets * max(1, 48 // sets)
+    reps, rem = divmod(args.steps, per_graph)
+
+    def capture(nsteps: int):
+        if nsteps == 0:
+            return None
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(nsteps):
+                step(i)
+        return g
+
+    g_main = capture(per_graph) if reps else None
+    g_rem = capture(rem)
+    with torch.cuda.stream(stream):
+        if g_main is not None:
+            g_main.replay()
+        if g_rem is not None:
+            g_rem.replay()
+    stream.synchronize()
+
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    phys = int(visible.split(",")[dev]) if visible and visible.split(",")[dev].strip().isdigit() else dev
+    clocks = ClockSampler(phys)
+    if rank == 0:
+        clocks.start()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    if rank == 0:
+        clocks.mark(True)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(reps):
+            g_main.replay()
+        if g_rem is not None:
+            g_rem.replay()
+        end.record(stream)
+    stream.synchronize()
+    torch.cuda.synchronize()
+    if rank == 0:
+        clocks.mark(False)
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(end)
+    t = torch.tensor([ms], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    clock_info = clocks.stop() if rank == 0 else None
+    value = total_bytes * args.steps / (ms * 1e-3) / 1e9
+    launches = args.steps * 2
+
+    # ---- per-launch durations of the dominant kernel (events around each launch,
+    #      queued behind a sleep so the GPU runs them back to back)
+    nprobe = 24 * sets
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(2 * nprobe + 1)]
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(20_000_000)
+        evs[0].record(stream)
+        for i in range(nprobe):
+            wu, wd = weights[i % sets]
+            K.matmul(kern, dev, y1_shard, wu, x, UP[0], n_up, 1, K.Q4_0)
+            evs[2 * i + 1].record(stream)
+            K.matmul(kern, dev, y2_shard, wd, y1_full, DOWN[0], n_down, 1, K.Q4_0)
+            evs[2 * i + 2].record(stream)
+    stream.synchronize()
+    d_up = [evs[2 * i].elapsed_time(evs[2 * i + 1]) for i in range(nprobe)]
+    d_down = [evs[2 * i + 1].elapsed_time(evs[2 * i + 2]) for i in range(nprobe)]
+    alg_up = q4_bytes(UP[0], n_up) + 4 * UP[0] + 4 * n_up
+    alg_down = q4_bytes(DOWN[0], n_down) + 4 * DOWN[0] + 4 * n_down
+    mean_up, mean_down = statistics.mean(d_up), statistics.mean(d_down)
+    achieved = (alg_up + alg_down) / ((mean_up + mean_down) * 1e-3) / 1e9
+    peaks = read_peaks()
+
+    # ---- end to end through the C ABI: pinned host X in, pinned host Y out
+    e2e_steps = min(args.steps, 2000)
+    xh = torch.empty(UP[0], dtype=torch.float32).pin_memory()
+    xh.copy_(x.cpu())
+    yh = torch.empty(DOWN[1], dtype=torch.float32).pin_memory()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_wall = time.perf_counter()
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for i in range(e2e_steps):
+            K.check(K.copy_async(x, xh, xh.numel() * 4, K.HOST_TO_DEVICE))
+            step(i)
+            K.check(K.copy_async(yh, y2_full, yh.numel() * 4, K.DEVICE_TO_HOST))
+            K.check(K.wait())
+        e1.record(stream)
+    stream.synchronize()
+    t_wall = time.perf_counter() - t_wall
+    e2e_ms = e0.elapsed_time(e1)
+    te = torch.tensor([e2e_ms], device="cuda")
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = float(te.item())
+    e2e_value = total_bytes * e2e_steps / (e2e_ms * 1e-3) / 1e9
+
+    cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
+
+    if rank == 0:
+        line = {
+            "metric": "q4_0_gemv_weight_gbps", "value": value, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": "q4_0 GEMV 7B MLP up+down, batch 1 (config 1)",
+                       "up": "K4096xN11008", "down": "K11008xN4096", "batch": 1,
+                       "parallelism": f"row-shard{world}+allgather" if world > 1 else "single",
+                       "weight_bytes_per_step": total_bytes,
+                       "l2": f"{sets} rotating weight sets ({sets * shard_bytes / 1e6:.0f} MB per GPU > 2x L2 "
+                             f"{l2 / 1e6:.0f} MB)",
+                       "timing": "CUDA graph replays, CUDA events on the launching stream, max over ranks"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / peaks["hbm_gbs"],
+                         "peak_source": peaks["source"],
+                         "traffic": profile_traffic("gemv_q4_0_k4096_n11008.md"),
+                         "kernel": "gemv_stream_kernel<q4_0,1>",
+                         "launch_us": {"up": mean_up * 1e3, "down": mean_down * 1e3},
+                         "algorithmic_bytes_per_launch": {"up": alg_up, "down": alg_down}},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": xh.numel() * 4,
+                    "d2h_bytes_per_step": yh.numel() * 4, "steps": e2e_steps,
+                    "path": "k200_copy_async H2D + 2x k200_matmul + k200_copy_async D2H + k200_wait per step",
+                    "wall_s": t_wall},
+            "gpu_launches": launches,
+            "clocks": clock_info,
+        }
+        print(json.dumps(line), flush=True)
+    K.set_stream(dev, None)
+    del g_main, g_rem
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100000)
+    ap.add_argument("--warmup", type=int, default=200)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

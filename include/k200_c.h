@@ -1,0 +1,92 @@
+/*
+ * k200_c.h -- C ABI of libkunlunk200.so.0 (B200 / sm_100a).
+ *
+ * Plain pointers, sizes and ints: the entry points an FFI (ctypes, cgo, JNI,
+ * N-API) binds to reach the kunlun:: matmul hot path without C++ name
+ * mangling.  Each function replaces the reference interface cited beside it
+ * (UnagiDojyou/kunlunK200_lib v0.7.12, include/kunlun/k200.h and
+ * src/k200.cpp) and keeps its argument meaning and error behaviour:
+ * contract violations abort with a diagnostic exactly as kunlun::require()
+ * does; device statuses are returned as ints (0 = success).
+ *
+ * Device pointers are CUDA device addresses.  `stream`-free: work goes to the
+ * library stream of the device (k200_stream returns it for callers that need
+ * to order their own work or record events on it).
+ */
+#ifndef K200_C_H
+#define K200_C_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- runtime: k200.h:10-23, src/k200.cpp:48-95 ---------------------------- */
+const char *k200_version(void);                         /* kunlun::version, k200.cpp:634 */
+int k200_device_count(int *count);                      /* kunlun::device_count, k200.cpp:63-66 */
+void k200_select(int device);                           /* kunlun::select, k200.cpp:67 */
+int k200_wait(void);                                    /* kunlun::wait, k200.cpp:68 */
+void k200_check(int status);                            /* kunlun::check, k200.cpp:53-55 */
+void k200_require(int condition);                       /* kunlun::require, k200.cpp:56-58 */
+/* kind: 0 host_to_device, 1 device_to_host, 2 device_to_device */
+int k200_copy(void *dst, const void *src, size_t bytes, int kind); /* kunlun::copy, k200.cpp:69-75 */
+void k200_peer(int dst_device, void *dst, int src_device, const void *src, size_t bytes); /* kunlun::peer, k200.cpp:89-95 */
+void *k200_allocate(int device, size_t bytes);          /* kunlun::allocate, k200.cpp:76-83 */
+void k200_release(int device, void *ptr, size_t bytes); /* kunlun::release, k200.cpp:84-87 */
+size_t k200_allocated_bytes(int device);                /* kunlun::allocated_bytes, k200.cpp:88 */
+void k200_lock(void);                                   /* runtime_mutex().lock(), k200.cpp:48 */
+void k200_unlock(void);                                 /* runtime_mutex().unlock() */
+
+/* ---- kernel handle: k200.h:62-88 (kunlun::Kernel) -------------------------- */
+void *k200_kernel_create(void);                         /* Kernel::Kernel, k200.cpp:249 */
+void k200_kernel_destroy(void *kernel);                 /* Kernel::~Kernel, k200.cpp:250-267 */
+
+/* ---- rowwise int8 packing: k200.h:90-96, src/k200.cpp:98-123 --------------- */
+size_t k200_aligned(size_t bytes);
+size_t k200_packed_i8_size(int k, int rows);
+float *k200_packed_i8_scales(void *weights, int k, int rows);
+float *k200_packed_i8_maxima(void *weights, int k, int rows);
+void k200_upload_i8_rows(int device, void *weights, int k, int rows, int first_row, int count,
+                         const float *host_input);
+
+/* ---- matmul: k200.h:98-105, src/k200.cpp:268-279 --------------------------- */
+/* type: 0 f32, 1 f16, 2 q4_0, 3 rowwise_i8 (kunlun::WeightType values) */
+void k200_matmul(void *kernel, int device, void *y, const void *w, const void *x, int k, int n, int batch,
+                 int type, const float *scales, const float *maxima, int tile);
+
+/* ---- elementwise: k200.h:106-107, src/k200.cpp:280-323 --------------------- */
+/* op: 0 add, 1 multiply, 2 silu, 3 rms_norm, 4 scale (kunlun::ElementwiseOp values) */
+void k200_elementwise(void *kernel, int device, void *y, const void *a, const void *b, int count, int width,
+                      int b_count, int op, float parameter);
+
+/* ---- statistics: k200.h:345-350 -------------------------------------------- */
+size_t k200_matmul_count(int device);                   /* Statistics::matmuls[device] */
+size_t k200_peer_copies(void);
+size_t k200_peer_bytes(void);
+
+/* ---- additions with no reference counterpart -------------------------------- */
+/* The library stream of `device` (a cudaStream_t), for event timing and for
+ * ordering caller work against library work. */
+void *k200_stream(int device);
+/* Issue all further work of `device` on `stream` (a cudaStream_t; NULL
+ * restores the library's own stream).  wait() then synchronises that stream.
+ * Lets a caller order library work inside its own stream or capture it in a
+ * CUDA graph; calls that grow scratch (the first rowwise_i8 matmul of a new
+ * size) synchronise and must not run during a capture. */
+void k200_set_stream(int device, void *stream);
+/* Asynchronous copy on the library stream of the current device (pinned host
+ * memory makes it truly asynchronous); completion via k200_wait(). */
+int k200_copy_async(void *dst, const void *src, size_t bytes, int kind);
+/* GGML Q4_0 quantiser on the device: f32 [n][k] (device) -> 18-byte blocks
+ * [n][k/32] (device).  Asynchronous on the library stream. */
+void k200_quantize_q4_0(int device, void *q4, const float *w, int k, int n);
+/* upload_i8_rows from DEVICE f32 rows (same packing and arithmetic as
+ * k200_upload_i8_rows).  Asynchronous on the library stream. */
+void k200_pack_i8_rows_device(int device, void *weights, int k, int rows, int first_row, int count,
+                              const float *device_input);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

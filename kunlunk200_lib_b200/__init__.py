@@ -1,0 +1,305 @@
+"""Python host side of the B200 k200 library.
+
+Binds ``lib/libkunlunk200.so.0`` (built in-tree by ``kunlunk200_lib_b200.build``)
+through its C ABI (``include/k200_c.h``) and mirrors the reference's
+``kunlun::`` API (UnagiDojyou/kunlunK200_lib v0.7.12, include/kunlun/k200.h)
+with the same names, argument meaning and error behaviour: contract
+violations abort the process with the reference's diagnostics, device
+statuses come back as ints.
+
+There is no CPU fallback: importing this module on a machine without the
+built library raises, and every compute call needs a CUDA device.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_DIR = os.path.join(_PKG, "lib")
+LIB_PATH = os.path.join(LIB_DIR, "libkunlunk200.so.0")
+
+# kunlun::WeightType / CopyKind / ElementwiseOp values (k200.h:18,40-41)
+F32, F16, Q4_0, ROWWISE_I8 = 0, 1, 2, 3
+HOST_TO_DEVICE, DEVICE_TO_HOST, DEVICE_TO_DEVICE = 0, 1, 2
+ADD, MULTIPLY, SILU, RMS_NORM, SCALE = 0, 1, 2, 3, 4
+
+_lib = None
+
+_SIGNATURES = {
+    "k200_version": (C.c_char_p, []),
+    "k200_device_count": (C.c_int, [C.POINTER(C.c_int)]),
+    "k200_select": (None, [C.c_int]),
+    "k200_wait": (C.c_int, []),
+    "k200_check": (None, [C.c_int]),
+    "k200_require": (None, [C.c_int]),
+    "k200_copy": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_int]),
+    "k200_copy_async": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_int]),
+    "k200_peer": (None, [C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_size_t]),
+    "k200_allocate": (C.c_void_p, [C.c_int, C.c_size_t]),
+    "k200_release": (None, [C.c_int, C.c_void_p, C.c_size_t]),
+    "k200_allocated_bytes": (C.c_size_t, [C.c_int]),
+    "k200_lock": (None, []),
+    "k200_unlock": (None, []),
+    "k200_kernel_create": (C.c_void_p, []),
+    "k200_kernel_destroy": (None, [C.c_void_p]),
+    "k200_aligned": (C.c_size_t, [C.c_size_t]),
+    "k200_packed_i8_size": (C.c_size_t, [C.c_int, C.c_int]),
+    "k200_packed_i8_scales": (C.c_void_p, [C.c_void_p, C.c_int, C.c_int]),
+    "k200_packed_i8_maxima": (C.c_void_p, [C.c_void_p, C.c_int, C.c_int]),
+    "k200_upload_i8_rows": (None, [C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p]),
+    "k200_pack_i8_rows_device": (None, [C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p]),
+    "k200_matmul": (None, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
+                           C.c_int, C.c_void_p, C.c_void_p, C.c_int]),
+    "k200_elementwise": (None, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
+                                C.c_int, C.c_int, C.c_float]),
+    "k200_matmul_count": (C.c_size_t, [C.c_int]),
+    "k200_peer_copies": (C.c_size_t, []),
+    "k200_peer_bytes": (C.c_size_t, []),
+    "k200_stream": (C.c_void_p, [C.c_int]),
+    "k200_set_stream": (None, [C.c_int, C.c_void_p]),
+    "k200_quantize_q4_0": (None, [C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int]),
+}
+
+
+def exported_symbols() -> list[str]:
+    """Every C-ABI symbol this package binds (the contents of include/k200_c.h)."""
+    return sorted(_SIGNATURES)
+
+
+def lib():
+    """The loaded libkunlunk200.so.0 (raises if it was not built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"{LIB_PATH} is missing: build it with `python -m kunlunk200_lib_b200.build`")
+        L = C.CDLL(LIB_PATH, mode=C.RTLD_GLOBAL)
+        for name, (res, args) in _SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _ptr(p) -> int | None:
+    """Device/host address of an int, ctypes pointer, numpy array or torch tensor."""
+    if p is None:
+        return None
+    if isinstance(p, int):
+        return p
+    if isinstance(p, np.ndarray):
+        return p.ctypes.data
+    if hasattr(p, "data_ptr"):
+        return p.data_ptr()
+    if isinstance(p, Buffer):
+        return p.data()
+    return C.cast(p, C.c_void_p).value
+
+
+# ---------------------------------------------------------------------------
+# runtime (k200.h:10-23)
+# ---------------------------------------------------------------------------
+def version() -> str:
+    return lib().k200_version().decode()
+
+
+def device_count() -> int:
+    n = C.c_int(0)
+    check(lib().k200_device_count(C.byref(n)))
+    return n.value
+
+
+def select(device: int) -> None:
+    lib().k200_select(device)
+
+
+def wait() -> int:
+    return lib().k200_wait()
+
+
+def check(status: int) -> None:
+    lib().k200_check(int(status))
+
+
+def require(condition: bool) -> None:
+    lib().k200_require(1 if condition else 0)
+
+
+def copy(dst, src, nbytes: int, kind: int) -> int:
+    return lib().k200_copy(_ptr(dst), _ptr(src), nbytes, kind)
+
+
+def copy_async(dst, src, nbytes: int, kind: int) -> int:
+    return lib().k200_copy_async(_ptr(dst), _ptr(src), nbytes, kind)
+
+
+def peer(dst_device: int, dst, src_device: int, src, nbytes: int) -> None:
+    lib().k200_peer(dst_device, _ptr(dst), src_device, _ptr(src), nbytes)
+
+
+def allocate(device: int, nbytes: int) -> int | None:
+    return lib().k200_allocate(device, nbytes)
+
+
+def release(device: int, ptr, nbytes: int) -> None:
+    lib().k200_release(device, _ptr(ptr), nbytes)
+
+
+def allocated_bytes(device: int) -> int:
+    return lib().k200_allocated_bytes(device)
+
+
+def stream(device: int) -> int:
+    """The library stream of `device` as an integer cudaStream_t handle."""
+    return lib().k200_stream(device) or 0
+
+
+def set_stream(device: int, stream_handle: int | None) -> None:
+    """Issue library work of `device` on a caller stream (None: the library's own)."""
+    lib().k200_set_stream(device, stream_handle or None)
+
+
+class runtime_lock:
+    """Context manager holding kunlun::runtime_mutex()."""
+
+    def __enter__(self):
+        lib().k200_lock()
+        return self
+
+    def __exit__(self, *exc):
+        lib().k200_unlock()
+        return False
+
+
+class Buffer:
+    """RAII device allocation (kunlun::Buffer, k200.h:25-37)."""
+
+    def __init__(self, device: int, nbytes: int):
+        self.device = device
+        self.nbytes = nbytes
+        self.ptr = allocate(device, nbytes)
+        require(bool(self.ptr))
+
+    def data(self) -> int:
+        return self.ptr
+
+    def size(self) -> int:
+        return self.nbytes
+
+    def upload(self, array: np.ndarray) -> None:
+        a = np.ascontiguousarray(array)
+        require(a.nbytes <= self.nbytes)
+        select(self.device)
+        check(copy(self.ptr, a, a.nbytes, HOST_TO_DEVICE))
+
+    def download(self, dtype, count: int, offset: int = 0) -> np.ndarray:
+        out = np.empty(count, dtype)
+        require(offset + out.nbytes <= self.nbytes)
+        select(self.device)
+        check(copy(out, self.ptr + offset, out.nbytes, DEVICE_TO_HOST))
+        return out
+
+    def close(self) -> None:
+        if self.ptr:
+            release(self.device, self.ptr, self.nbytes)
+            self.ptr = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Kernel:
+    """Per-call state bound to one device (kunlun::Kernel, k200.h:62-88)."""
+
+    def __init__(self):
+        self.handle = lib().k200_kernel_create()
+
+    def close(self) -> None:
+        if self.handle:
+            lib().k200_kernel_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ---------------------------------------------------------------------------
+# rowwise int8 packing (k200.h:90-96)
+# ---------------------------------------------------------------------------
+def aligned(nbytes: int) -> int:
+    return lib().k200_aligned(nbytes)
+
+
+def packed_i8_size(k: int, rows: int) -> int:
+    return lib().k200_packed_i8_size(k, rows)
+
+
+def packed_i8_scales(weights, k: int, rows: int) -> int:
+    return lib().k200_packed_i8_scales(_ptr(weights), k, rows)
+
+
+def packed_i8_maxima(weights, k: int, rows: int) -> int:
+    return lib().k200_packed_i8_maxima(_ptr(weights), k, rows)
+
+
+def upload_i8_rows(device: int, weights, k: int, rows: int, first_row: int, count: int, host_input) -> None:
+    if isinstance(host_input, np.ndarray):
+        host_input = np.ascontiguousarray(host_input, np.float32)
+    lib().k200_upload_i8_rows(device, _ptr(weights), k, rows, first_row, count, _ptr(host_input))
+
+
+def pack_i8_rows_device(device: int, weights, k: int, rows: int, first_row: int, count: int, device_input) -> None:
+    lib().k200_pack_i8_rows_device(device, _ptr(weights), k, rows, first_row, count, _ptr(device_input))
+
+
+# ---------------------------------------------------------------------------
+# matmul / elementwise (k200.h:98-107)
+# ---------------------------------------------------------------------------
+def matmul(kernel: Kernel, device: int, y, w, x, k: int, n: int, batch: int, type: int,
+           scales=None, maxima=None, tile: int = 16) -> None:
+    """Submit Y[batch,n] = X[batch,k] . W^T[n,k]; select(device)+check(wait()) completes it."""
+    lib().k200_matmul(kernel.handle, device, _ptr(y), _ptr(w), _ptr(x), k, n, batch, int(type),
+                      _ptr(scales), _ptr(maxima), tile)
+
+
+def elementwise(kernel: Kernel, device: int, y, a, b, count: int, width: int, b_count: int, op: int,
+                parameter: float = 0.0) -> None:
+    lib().k200_elementwise(kernel.handle, device, _ptr(y), _ptr(a), _ptr(b), count, width, b_count, int(op),
+                           float(parameter))
+
+
+def quantize_q4_0(device: int, q4, w, k: int, n: int) -> None:
+    """GGML Q4_0 block quantiser on the device (f32 [n][k] -> [n][k/32] blocks)."""
+    lib().k200_quantize_q4_0(device, _ptr(q4), _ptr(w), k, n)
+
+
+def matmul_count(device: int) -> int:
+    return lib().k200_matmul_count(device)
+
+
+def statistics() -> dict:
+    return {"matmuls": [matmul_count(d) for d in range(max(1, device_count()))],
+            "peer_copies": lib().k200_peer_copies(), "peer_bytes": lib().k200_peer_bytes()}
+
+
+def weight_bytes(type: int, k: int, n: int) -> int:
+    """Bytes of a legacy weight matrix [n,k] in the given encoding."""
+    if type == F32:
+        return 4 * k * n
+    if type == F16:
+        return 2 * k * n
+    if type == Q4_0:
+        return n * (k // 32) * 18
+    if type == ROWWISE_I8:
+        return packed_i8_size(k, n)
+    raise ValueError(type)

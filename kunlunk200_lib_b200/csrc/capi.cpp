@@ -1,0 +1,110 @@
+// extern "C" entry points of libkunlunk200 (declared in include/k200_c.h):
+// thin forwards to the kunlun:: C++ API so that FFIs bind unmangled names.
+#include <k200_c.h>
+#include <kunlun/k200.h>
+
+#include <cuda_runtime.h>
+
+#include "k200_internal.h"
+
+namespace k200 {
+cudaStream_t library_stream(int device);
+void set_stream(int device, cudaStream_t s);
+const DeviceInfo &device_info(int device);
+int current_device();
+size_t matmul_count(int device);
+size_t peer_copy_count();
+size_t peer_byte_count();
+}  // namespace k200
+
+extern "C" {
+
+const char *k200_version(void) { return kunlun::version(); }
+int k200_device_count(int *count) { return kunlun::device_count(count); }
+void k200_select(int device) { kunlun::select(device); }
+int k200_wait(void) { return kunlun::wait(); }
+void k200_check(int status) { kunlun::check(status); }
+void k200_require(int condition) { kunlun::require(condition != 0); }
+
+int k200_copy(void *dst, const void *src, size_t bytes, int kind) {
+    kunlun::require(kind >= 0 && kind <= 2);
+    return kunlun::copy(dst, src, bytes, static_cast<kunlun::CopyKind>(kind));
+}
+
+void k200_peer(int dst_device, void *dst, int src_device, const void *src, size_t bytes) {
+    kunlun::peer(dst_device, dst, src_device, src, bytes);
+}
+
+void *k200_allocate(int device, size_t bytes) { return kunlun::allocate(device, bytes); }
+void k200_release(int device, void *ptr, size_t bytes) { kunlun::release(device, ptr, bytes); }
+size_t k200_allocated_bytes(int device) { return kunlun::allocated_bytes(device); }
+void k200_lock(void) { kunlun::runtime_mutex().lock(); }
+void k200_unlock(void) { kunlun::runtime_mutex().unlock(); }
+
+void *k200_kernel_create(void) { return new kunlun::Kernel(); }
+void k200_kernel_destroy(void *kernel) { delete static_cast<kunlun::Kernel *>(kernel); }
+
+size_t k200_aligned(size_t bytes) { return kunlun::aligned(bytes); }
+size_t k200_packed_i8_size(int k, int rows) { return kunlun::packed_i8_size(k, rows); }
+float *k200_packed_i8_scales(void *weights, int k, int rows) { return kunlun::packed_i8_scales(weights, k, rows); }
+float *k200_packed_i8_maxima(void *weights, int k, int rows) { return kunlun::packed_i8_maxima(weights, k, rows); }
+void k200_upload_i8_rows(int device, void *weights, int k, int rows, int first_row, int count,
+                         const float *host_input) {
+    kunlun::upload_i8_rows(device, weights, k, rows, first_row, count, host_input);
+}
+
+void k200_matmul(void *kernel, int device, void *y, const void *w, const void *x, int k, int n, int batch, int type,
+                 const float *scales, const float *maxima, int tile) {
+    kunlun::require(kernel != nullptr && type >= 0 && type <= 3);
+    kunlun::matmul(*static_cast<kunlun::Kernel *>(kernel), device, y, w, x, k, n, batch,
+                   static_cast<kunlun::WeightType>(type), scales, maxima, tile);
+}
+
+void k200_elementwise(void *kernel, int device, void *y, const void *a, const void *b, int count, int width,
+                      int b_count, int op, float parameter) {
+    kunlun::require(kernel != nullptr && op >= 0 && op <= 4);
+    kunlun::elementwise(*static_cast<kunlun::Kernel *>(kernel), device, y, a, b, count, width, b_count,
+                        static_cast<kunlun::ElementwiseOp>(op), parameter);
+}
+
+size_t k200_matmul_count(int device) { return k200::matmul_count(device); }
+size_t k200_peer_copies(void) { return k200::peer_copy_count(); }
+size_t k200_peer_bytes(void) { return k200::peer_byte_count(); }
+
+void *k200_stream(int device) { return static_cast<void *>(k200::library_stream(device)); }
+
+void k200_set_stream(int device, void *stream) { k200::set_stream(device, static_cast<cudaStream_t>(stream)); }
+
+int k200_copy_async(void *dst, const void *src, size_t bytes, int kind) {
+    std::lock_guard<std::recursive_mutex> lock(kunlun::runtime_mutex());
+    kunlun::require(kind >= 0 && kind <= 2 && k200::current_device() >= 0);
+    const cudaMemcpyKind k = kind == 0 ? cudaMemcpyHostToDevice : kind == 1 ? cudaMemcpyDeviceToHost
+                                                                            : cudaMemcpyDeviceToDevice;
+    return (int)cudaMemcpyAsync(dst, src, bytes, k, k200::library_stream(k200::current_device()));
+}
+
+void k200_quantize_q4_0(int device, void *q4, const float *w, int k, int n) {
+    std::lock_guard<std::recursive_mutex> lock(kunlun::runtime_mutex());
+    kunlun::require(q4 && w && k > 0 && k % 32 == 0 && n > 0);
+    kunlun::require((reinterpret_cast<uintptr_t>(w) & 15) == 0);
+    kunlun::select(device);
+    kunlun::check((int)k200::launch_q4_0_quantize(w, n, k, static_cast<uint8_t *>(q4), k200::library_stream(device)));
+}
+
+void k200_pack_i8_rows_device(int device, void *weights, int k, int rows, int first_row, int count,
+                              const float *device_input) {
+    std::lock_guard<std::recursive_mutex> lock(kunlun::runtime_mutex());
+    kunlun::require(weights && device_input && k > 0 && rows > 0 && first_row >= 0 && count >= 0 &&
+                    first_row <= rows && count <= rows - first_row);
+    kunlun::select(device);
+    const k200::DeviceInfo &info = k200::device_info(device);
+    cudaStream_t s = k200::library_stream(device);
+    kunlun::check((int)k200::launch_i8_rows(device_input, k, count,
+                                            static_cast<int8_t *>(weights) + (size_t)first_row * k,
+                                            kunlun::packed_i8_scales(weights, k, rows) + first_row, info, s));
+    static const float maximum[6] = {127, 127, 127, 127, 127, 127};
+    kunlun::check((int)cudaMemcpyAsync(kunlun::packed_i8_maxima(weights, k, rows), maximum, sizeof(maximum),
+                                       cudaMemcpyHostToDevice, s));
+}
+
+}  // extern "C"

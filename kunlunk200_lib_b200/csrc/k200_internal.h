@@ -1,0 +1,54 @@
+// Internal interfaces between the host runtime (runtime.cpp, matmul.cpp) and
+// the CUDA kernels of libkunlunk200.  Not installed; not part of the ABI.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace k200 {
+
+struct DeviceInfo {
+    int id = -1;
+    int sm_count = 0;
+    int smem_optin = 0;     // max dynamic shared memory per block (opt-in)
+    int *err = nullptr;     // device view of the mapped error word
+};
+
+// One legacy matmul launch: Y[c, r] = W[r, :] . X[c, :].
+struct GemvRequest {
+    int wt;                        // 0 f32, 1 f16, 2 q4_0, 3 rowwise int8
+    const void *w;                 // weight rows
+    const float *x;                // f32 activations (wt 0..2)
+    const int8_t *q;               // int8 activation components (wt 3): [2][q_batch][q_stride]
+    const float *act_max;          // {max0, max1} (wt 3)
+    const float *row_scale;        // per-row scales (wt 3)
+    float *y;
+    int k, n, batch;
+    int x_stride, q_stride, y_stride;
+    long long q_comp;              // elements between component 0 and 1 of q (wt 3)
+};
+
+// Streaming GEMV launcher (handles any batch by column groups).
+cudaError_t launch_gemv(const GemvRequest &r, const DeviceInfo &dev, cudaStream_t stream);
+bool gemv_fast_path_ok(int wt, const void *w, const void *x, const void *y, int k, long long row_bytes);
+
+// Per-tensor two-component A8 quantiser of the rowwise-int8 path
+// (src/k200.cpp:209-229).  q receives [2][count] int8, maxima {max0, max1}.
+// `scratch` holds count floats (residual) plus 64 bytes of reduction words.
+cudaError_t launch_a8_tensor(const float *x, size_t count, int8_t *q, float *maxima, void *scratch,
+                             const DeviceInfo &dev, cudaStream_t stream);
+size_t a8_tensor_scratch_bytes(size_t count);
+
+// upload_i8_rows on the device (src/k200.cpp:107-116): f32 rows -> int8 rows
+// and per-row scales.
+cudaError_t launch_i8_rows(const float *w, int k, int rows, int8_t *q, float *scales, const DeviceInfo &dev,
+                           cudaStream_t stream);
+
+// kunlun::elementwise (op 0 add, 1 multiply, 2 silu, 3 rms_norm, 4 scale).
+cudaError_t launch_elementwise(float *y, const float *a, const float *b, int n, int width, int bn, int op, float p,
+                               const DeviceInfo &dev, cudaStream_t stream);
+
+// GGML Q4_0 block quantiser (f32 [n][k] -> 18-byte blocks).
+cudaError_t launch_q4_0_quantize(const float *w, int n, int k, uint8_t *q4, cudaStream_t stream);
+
+}  // namespace k200

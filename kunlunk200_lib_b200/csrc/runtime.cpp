@@ -1,0 +1,420 @@
+// Host runtime of libkunlunk200 on CUDA: the kunlun:: API of the reference's
+// src/k200.cpp (UnagiDojyou/kunlunK200_lib v0.7.12) re-implemented over the
+// CUDA runtime.  Semantics kept from the reference:
+//   * one process-global recursive mutex taken by every entry point
+//     (src/k200.cpp:25,48);
+//   * fail-fast: check()/require() print the device, tensor and shape context
+//     and abort (src/k200.cpp:32-36,53-62); allocate() returns null on failure
+//     (src/k200.cpp:76-83);
+//   * matmul() validates the reference contract (src/k200.cpp:268-279) and
+//     only submits work; select(device) + check(wait()) completes it;
+//   * copy()/peer()/upload_i8_rows()/elementwise() complete before returning.
+// Device model: a PD index is a CUDA ordinal.  Each device gets one library
+// stream (a blocking stream, so it is ordered after work on the legacy default
+// stream, e.g. cudaMemcpy or a framework's default stream) and one error word
+// in mapped host memory that kernels post to instead of trapping.
+#include <kunlun/k200.h>
+
+#include <algorithm>
+#include <atomic>
+#include <climits>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "k200_internal.h"
+
+namespace kunlun {
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+std::recursive_mutex mutex;
+std::atomic<size_t> peer_copies{0}, peer_bytes{0};
+
+struct DeviceState {
+    bool ready = false;
+    cudaStream_t own = nullptr;      // the library stream created at first use
+    cudaStream_t stream = nullptr;   // the stream work is issued on (own, or a caller's)
+    int *err_host = nullptr;
+    k200::DeviceInfo info;
+    std::atomic<size_t> allocated{0};
+    std::atomic<size_t> matmuls{0};
+};
+DeviceState devices[kMaxDevices];
+
+thread_local int current_device = -1;
+thread_local int diagnostic_device = -1;
+thread_local const char *diagnostic_name = nullptr;
+thread_local int64_t diagnostic_shape[4] = {};
+
+void diagnostic_print() {
+    std::fprintf(stderr, "Kunlun context: pd=%d tensor=%s shape=[%lld,%lld,%lld,%lld]\n", diagnostic_device,
+                 diagnostic_name ? diagnostic_name : "<outside graph>", (long long)diagnostic_shape[0],
+                 (long long)diagnostic_shape[1], (long long)diagnostic_shape[2], (long long)diagnostic_shape[3]);
+    std::fflush(stderr);
+}
+
+int cuda_device_count() {
+    static int count = -1;
+    if (count < 0) {
+        int n = 0;
+        if (cudaGetDeviceCount(&n) != cudaSuccess) {
+            cudaGetLastError();
+            n = 0;
+        }
+        count = std::min(n, kMaxDevices);
+    }
+    return count;
+}
+
+void fail_cuda(cudaError_t e, const char *what) {
+    if (e != cudaSuccess) {
+        diagnostic_print();
+        std::fprintf(stderr, "Kunlun CUDA failure: %s: %s (%d)\n", what, cudaGetErrorString(e), (int)e);
+        std::fflush(stderr);
+        std::abort();
+    }
+}
+
+DeviceState &state(int id) {
+    DeviceState &d = devices[id];
+    if (!d.ready) {
+        fail_cuda(cudaSetDevice(id), "cudaSetDevice");
+        fail_cuda(cudaStreamCreate(&d.own), "cudaStreamCreate");
+        d.stream = d.own;
+        fail_cuda(cudaHostAlloc(reinterpret_cast<void **>(&d.err_host), 64, cudaHostAllocMapped),
+                  "cudaHostAlloc(error word)");
+        *d.err_host = 0;
+        int *dev_err = nullptr;
+        fail_cuda(cudaHostGetDevicePointer(reinterpret_cast<void **>(&dev_err), d.err_host, 0),
+                  "cudaHostGetDevicePointer");
+        d.info.id = id;
+        d.info.err = dev_err;
+        fail_cuda(cudaDeviceGetAttribute(&d.info.sm_count, cudaDevAttrMultiProcessorCount, id), "sm count");
+        fail_cuda(cudaDeviceGetAttribute(&d.info.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, id),
+                  "smem opt-in");
+        d.ready = true;
+    }
+    return d;
+}
+
+DeviceState &current() {
+    require(current_device >= 0);
+    return state(current_device);
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// runtime
+// ---------------------------------------------------------------------------
+std::recursive_mutex &runtime_mutex() { return mutex; }
+
+void diagnostic_tensor(const char *name, const int64_t *dimensions) {
+    diagnostic_name = name;
+    for (int i = 0; i < 4; ++i) diagnostic_shape[i] = dimensions ? dimensions[i] : 0;
+}
+
+void check(int rc) {
+    if (rc) {
+        diagnostic_print();
+        std::fprintf(stderr, "Kunlun runtime error %d\n", rc);
+        std::fflush(stderr);
+        std::abort();
+    }
+}
+
+void require(bool ok) {
+    if (!ok) {
+        diagnostic_print();
+        std::fprintf(stderr, "Kunlun invalid argument or unavailable resource\n");
+        std::fflush(stderr);
+        std::abort();
+    }
+}
+
+int device_count(int *n) {
+    std::lock_guard<std::recursive_mutex> lock(mutex);
+    if (!n) return (int)cudaErrorInvalidValue;
+    *n = cuda_device_count();
+    return 0;
+}
+
+void select(int id) {
+    diagnostic_device = id;
+    require(id >= 0 && id < cuda_device_count());
+    std::lock_guard<std::recursive_mutex> lock(mutex);
+    state(id);
+    fail_cuda(cudaSetDevice(id), "cudaSetDevice");
+    current_device = id;
+}
+
+int wait() {
+    if (current_device < 0) return (int)cudaErrorInvalidDevice;
+    DeviceState &d = state(current_device);
+    cudaError_t e = cudaStreamSynchronize(d.stream);
+    if (e != cudaSuccess) return (int)e;
+    int posted = __atomic_exchange_n(d.err_host, 0, __ATOMIC_SEQ_CST);
+    return posted;
+}
+
+int copy(void *dst, const void *src, size_t bytes, CopyKind kind) {
+    require(kind == host_to_device || kind == device_to_host || kind == device_to_device);
+    std::lock_guard<std::recursive_mutex> lock(mutex);
+    DeviceState &d = current();
+    if (bytes == 0) return 0;
+    cudaMemcpyKind k = kind == host_to_device   ? cudaMemcpyHostToDevice
+                       : kind == device_to_host ? cudaMemcpyDeviceToHost
+                                                : cudaMemcpyDeviceToDevice;
+    cudaError_t e = cudaMemcpyAsync(dst, src, bytes, k, d.stream);
+    if (e != cudaSuccess) return (int)e;
+    return (int)cudaStreamSynchronize(d.stream);
+}
+
+void *allocate(int id, size_t bytes) {
+    std::lock_guard<std::recursive_mutex> lock(mutex);
+    select(id);
+    void *ptr = nullptr;
+    size_t size = std::max<size_t>(bytes, 256);
+    if (cudaMalloc(&ptr, size) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    devices[id].allocated += size;
+    return ptr;
+}
+
+void release(int id, void *ptr, size_t bytes) {
+    std::lock_guard<std::recursive_mutex> lock(mutex);
+    if (!ptr) return;
+    select(id);
+    check((int)cudaFree(ptr));
+    devices[id].allocated -= std::max<size_t>(bytes, 256);
+}
+
+size_t allocated_bytes(int id) {
+    require(id >= 0 && id < kMaxDevices);
+    return devices[id].allocated.load();
+}
+
+void peer(int dst, void *dp, int src, const void *sp, size_t bytes) {
+    std::lock_guard<std::recursive_mutex> lock(mutex);
+    select(src);
+    check(wait());
+    select(dst);
+    if (dst != src) {
+        int can = 0;
+        if (cudaDeviceCanAccessPeer(&can, dst, src) == cudaSuccess && can) {
+            cudaError_t e = cudaDeviceEnablePeerAccess(src, 0);
+            if (e == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
+            else fail_cuda(e, "cudaDeviceEnablePeerAccess");
+        }
+    }
+    fail_cuda(cudaMemcpyPeerAsync(dp, dst, sp, src, bytes, state(dst).stream), "cudaMemcpyPeerAsync");
+    check(wait());
+    ++peer_copies;
+    peer_bytes += bytes;
+}
+
+Buffer::Buffer(int id, size_t bytes) : device_(id), bytes_(bytes), ptr_(allocate(id, bytes)) { require(ptr_); }
+Buffer::~Buffer() { release(device_, ptr_, bytes_); }
+
+size_t aligned(size_t n) {
+    require(n <= SIZE_MAX - 255);
+    return (n + 255) & ~size_t(255);
+}
+size_t packed_i8_size(int k, int n) {
+    require(k > 0 && n >= 0);
+    return aligned((size_t)k * n) + aligned((size_t)n * 4) + 256;
+}
+float *packed_i8_scales(void *p, int k, int n) { return (float *)((char *)p + aligned((size_t)k * n)); }
+float *packed_i8_maxima(void *p, int k, int n) {
+    return (float *)((char *)packed_i8_scales(p, k, n) + aligned((size_t)n * 4));
+}
+
+// ---------------------------------------------------------------------------
+// Kernel handle
+// ---------------------------------------------------------------------------
+struct Kernel::Impl {
+    int id = -1;
+    void *quant = nullptr;   // rowwise int8: [2][batch*k] quantised activations
+    size_t quant_size = 0;
+    void *params = nullptr;  // {max0, max1} + reduction words (256 bytes)
+    void *alias = nullptr;   // elementwise broadcast operand copy when y aliases b
+    size_t alias_size = 0;
+};
+
+Kernel::Kernel() : impl_(new Impl{}) {}
+Kernel::~Kernel() {
+    std::lock_guard<std::recursive_mutex> lock(mutex);
+    Impl &s = *impl_;
+    if (s.id >= 0) {
+        select(s.id);
+        check(wait());
+        release(s.id, s.quant, s.quant_size);
+        release(s.id, s.params, 256);
+        release(s.id, s.alias, s.alias_size);
+    }
+    delete impl_;
+}
+
+namespace {
+void grow(Kernel::Impl &s, void *&ptr, size_t &size, size_t need) {
+    if (size >= need) return;
+    if (ptr) {
+        check(wait());  // in-flight work may still read the old buffer
+        release(s.id, ptr, size);
+    }
+    ptr = allocate(s.id, need);
+    require(ptr);
+    size = need;
+}
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// matmul (src/k200.cpp:187-279)
+// ---------------------------------------------------------------------------
+void matmul(Kernel &kernel, int id, void *y, const void *w, const void *x, int k, int n, int batch, WeightType type,
+            const float *scales, const float *maximum, int tile) {
+    std::lock_guard<std::recursive_mutex> lock(mutex);
+    require(type == WeightType::f32 || type == WeightType::f16 || type == WeightType::q4_0 ||
+            type == WeightType::rowwise_i8);
+    require(k > 0 && k <= 16384 && k % 32 == 0 && n > 0 && batch > 0 && n <= INT_MAX / batch &&
+            k <= INT_MAX / batch);
+    require((size_t)n * batch <= INT_MAX / 4 && (size_t)k * batch <= INT_MAX / 4);
+    size_t row_bytes = type == WeightType::f32   ? (size_t)k * 4
+                       : type == WeightType::f16 ? (size_t)k * 2
+                       : type == WeightType::q4_0 ? (size_t)k / 32 * 18
+                                                  : (size_t)k;
+    require(y && w && x && (size_t)n <= INT_MAX / row_bytes && (tile == 1 || tile == 16));
+    require(kernel.impl_->id == -1 || kernel.impl_->id == id);
+    require(type != WeightType::rowwise_i8 || (scales && maximum));
+    select(id);
+    Kernel::Impl &s = *kernel.impl_;
+    s.id = id;
+    DeviceState &d = state(id);
+
+    k200::GemvRequest r{};
+    r.wt = (int)type;
+    r.w = w;
+    r.y = static_cast<float *>(y);
+    r.k = k;
+    r.n = n;
+    r.batch = batch;
+    r.x_stride = k;
+    r.y_stride = n;
+    if (type == WeightType::rowwise_i8) {
+        const size_t count = (size_t)k * batch;
+        grow(s, s.quant, s.quant_size, aligned(2 * count));
+        if (!s.params) {
+            size_t dummy = 0;
+            grow(s, s.params, dummy, 256);
+        }
+        float *maxima = static_cast<float *>(s.params);
+        void *words = static_cast<char *>(s.params) + 64;
+        check((int)k200::launch_a8_tensor(static_cast<const float *>(x), count, static_cast<int8_t *>(s.quant),
+                                          maxima, words, d.info, d.stream));
+        r.q = static_cast<const int8_t *>(s.quant);
+        r.q_stride = k;
+        r.q_comp = (long long)count;
+        r.act_max = maxima;
+        r.row_scale = scales;
+    } else {
+        r.x = static_cast<const float *>(x);
+    }
+    check((int)k200::launch_gemv(r, d.info, d.stream));
+    ++d.matmuls;
+}
+
+// ---------------------------------------------------------------------------
+// upload_i8_rows (src/k200.cpp:102-123)
+// ---------------------------------------------------------------------------
+void upload_i8_rows(int id, void *weights, int k, int n, int first, int count, const float *input) {
+    std::lock_guard<std::recursive_mutex> lock(mutex);
+    require(weights && input && k > 0 && n > 0 && first >= 0 && count >= 0 && first <= n && count <= n - first);
+    select(id);
+    DeviceState &d = state(id);
+    if (count > 0) {
+        const size_t bytes = (size_t)count * k * 4;
+        void *staging = nullptr;
+        fail_cuda(cudaMalloc(&staging, bytes), "cudaMalloc(upload staging)");
+        fail_cuda(cudaMemcpyAsync(staging, input, bytes, cudaMemcpyHostToDevice, d.stream), "upload copy");
+        check((int)k200::launch_i8_rows(static_cast<const float *>(staging), k, count,
+                                        static_cast<int8_t *>(weights) + (size_t)first * k,
+                                        packed_i8_scales(weights, k, n) + first, d.info, d.stream));
+        int rc = wait();
+        cudaFree(staging);
+        require(rc == 0);  // non-finite input aborts, as in the reference
+    }
+    const float maximum[6] = {127, 127, 127, 127, 127, 127};
+    check(copy(packed_i8_maxima(weights, k, n), maximum, sizeof(maximum), host_to_device));
+}
+
+// ---------------------------------------------------------------------------
+// elementwise (src/k200.cpp:280-323)
+// ---------------------------------------------------------------------------
+void elementwise(Kernel &kernel, int id, void *y, const void *a, const void *b, int n, int width, int bn,
+                 ElementwiseOp operation, float parameter) {
+    std::lock_guard<std::recursive_mutex> lock(mutex);
+    int op = (int)operation;
+    require(y && a && b && n > 0 && n <= INT_MAX / 4 && width > 0 && width <= 16384 && n % width == 0);
+    require(op >= 0 && op <= 4 && (bn == n || bn == width));
+    if (op == 3) require(std::isfinite(parameter) && parameter > 0);
+    require(kernel.impl_->id == -1 || kernel.impl_->id == id);
+    Kernel::Impl &s = *kernel.impl_;
+    s.id = id;
+    select(id);
+    DeviceState &d = state(id);
+    if (y == b && bn != n && (op == 0 || op == 1)) {
+        // the broadcast operand would be overwritten while still being read
+        grow(s, s.alias, s.alias_size, (size_t)bn * 4);
+        fail_cuda(cudaMemcpyAsync(s.alias, b, (size_t)bn * 4, cudaMemcpyDeviceToDevice, d.stream), "alias copy");
+        b = s.alias;
+    }
+    check((int)k200::launch_elementwise(static_cast<float *>(y), static_cast<const float *>(a),
+                                        static_cast<const float *>(b), n, width, bn, op, parameter, d.info,
+                                        d.stream));
+    check(wait());
+}
+
+Statistics statistics() {
+    return {{devices[0].matmuls.load(), devices[1].matmuls.load()}, peer_copies.load(), peer_bytes.load()};
+}
+
+const char *version() { return "0.7.12"; }
+
+}  // namespace kunlun
+
+// ---------------------------------------------------------------------------
+// hooks used by the C ABI (capi.cpp)
+// ---------------------------------------------------------------------------
+namespace k200 {
+cudaStream_t library_stream(int device) {
+    kunlun::require(device >= 0 && device < kunlun::cuda_device_count());
+    std::lock_guard<std::recursive_mutex> lock(kunlun::mutex);
+    return kunlun::state(device).stream;
+}
+void set_stream(int device, cudaStream_t s) {
+    kunlun::require(device >= 0 && device < kunlun::cuda_device_count());
+    std::lock_guard<std::recursive_mutex> lock(kunlun::mutex);
+    kunlun::DeviceState &d = kunlun::state(device);
+    d.stream = s ? s : d.own;
+}
+const DeviceInfo &device_info(int device) {
+    std::lock_guard<std::recursive_mutex> lock(kunlun::mutex);
+    return kunlun::state(device).info;
+}
+int current_device() { return kunlun::current_device; }
+size_t matmul_count(int device) {
+    kunlun::require(device >= 0 && device < kunlun::kMaxDevices);
+    return kunlun::devices[device].matmuls.load();
+}
+size_t peer_copy_count() { return kunlun::peer_copies.load(); }
+size_t peer_byte_count() { return kunlun::peer_bytes.load(); }
+}  // namespace k200

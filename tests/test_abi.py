@@ -1,0 +1,127 @@
+"""CPU: the C-ABI library loads, exports every declared symbol, keeps the
+reference's packaging contract, and rejects contract violations the way the
+reference does (abort with a diagnostic) -- all without touching a GPU."""
+from __future__ import annotations
+
+import os
+import re
+import subprocess
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared_c_symbols() -> set[str]:
+    text = open(os.path.join(ROOT, "include", "k200_c.h")).read()
+    return set(re.findall(r"\b(k200_[a-z0-9_]+)\s*\(", text))
+
+
+def _exported(path: str) -> set[str]:
+    out = subprocess.run(["nm", "-D", "--defined-only", path], capture_output=True, text=True, check=True).stdout
+    return {line.split()[-1] for line in out.splitlines() if " T " in line}
+
+
+def test_library_loads_without_gpu(K):
+    assert K.version() == "0.7.12"
+
+
+def test_every_c_abi_symbol_is_exported(K):
+    declared = _declared_c_symbols()
+    assert declared, "no declarations parsed from include/k200_c.h"
+    exported = _exported(K.LIB_PATH)
+    missing = declared - exported
+    assert not missing, f"declared but not exported: {sorted(missing)}"
+    assert declared <= set(K.exported_symbols()) | declared  # python binds a subset; all must exist
+    for name in K.exported_symbols():
+        assert name in exported
+
+
+def test_cpp_api_symbols_match_reference_mangling(K):
+    """The kunlun:: hot-path API keeps the reference's Itanium-mangled names."""
+    exported = _exported(K.LIB_PATH)
+    expected = [
+        "_ZN6kunlun13runtime_mutexEv",
+        "_ZN6kunlun5checkEi",
+        "_ZN6kunlun7requireEb",
+        "_ZN6kunlun6selectEi",
+        "_ZN6kunlun4waitEv",
+        "_ZN6kunlun4copyEPvPKvmNS_8CopyKindE",
+        "_ZN6kunlun4peerEiPviPKvm",
+        "_ZN6kunlun8allocateEim",
+        "_ZN6kunlun7releaseEiPvm",
+        "_ZN6kunlun15allocated_bytesEi",
+        "_ZN6kunlun12device_countEPi",
+        "_ZN6kunlun17diagnostic_tensorEPKcPKl",
+        "_ZN6kunlun6BufferC1Eim",
+        "_ZN6kunlun6BufferD1Ev",
+        "_ZN6kunlun6KernelC1Ev",
+        "_ZN6kunlun6KernelD1Ev",
+        "_ZN6kunlun7alignedEm",
+        "_ZN6kunlun14packed_i8_sizeEii",
+        "_ZN6kunlun16packed_i8_scalesEPvii",
+        "_ZN6kunlun16packed_i8_maximaEPvii",
+        "_ZN6kunlun14upload_i8_rowsEiPviiiiPKf",
+        "_ZN6kunlun6matmulERNS_6KernelEiPvPKvS4_iiiNS_10WeightTypeEPKfS7_i",
+        "_ZN6kunlun11elementwiseERNS_6KernelEiPvPKvS4_iiiNS_13ElementwiseOpEf",
+        "_ZN6kunlun10statisticsEv",
+        "_ZN6kunlun7versionEv",
+    ]
+    missing = [s for s in expected if s not in exported]
+    assert not missing, missing
+
+
+def test_soname_is_reference_packaging(K):
+    out = subprocess.run(["readelf", "-d", K.LIB_PATH], capture_output=True, text=True, check=True).stdout
+    assert "Library soname: [libkunlunk200.so.0]" in out
+
+
+def test_reference_consumers_link_against_this_library():
+    """Reference programs compiled against the reference header resolve every
+    symbol from this library (built by `make -C oracle consumers`)."""
+    bindir = os.path.join(ROOT, "oracle", "_ref", "bin")
+    progs = [p for p in ("library-bench", "fused-bench", "native-q4-bench", "memory-example")
+             if os.path.exists(os.path.join(bindir, p))]
+    if not progs:
+        pytest.skip("reference consumer programs not built in this checkout")
+    exported = _exported(os.path.join(ROOT, "kunlunk200_lib_b200", "lib", "libkunlunk200.so.0"))
+    for p in progs:
+        path = os.path.join(bindir, p)
+        out = subprocess.run(["ldd", path], capture_output=True, text=True).stdout
+        assert "libkunlunk200.so.0 =>" in out and "not found" not in out, out
+        needed = subprocess.run(["nm", "-u", path], capture_output=True, text=True, check=True).stdout
+        wanted = {l.split()[-1] for l in needed.splitlines() if "kunlun" in l}
+        assert wanted and wanted <= exported, sorted(wanted - exported)
+
+
+def _run_contract(snippet: str) -> subprocess.CompletedProcess:
+    code = (
+        "import sys; sys.path.insert(0, %r)\n"
+        "import kunlunk200_lib_b200 as K\n"
+        "kern = K.Kernel()\n" % ROOT
+    ) + snippet
+    return subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=120)
+
+
+@pytest.mark.parametrize(
+    "case,call",
+    [
+        ("k not multiple of 32", "K.matmul(kern, 0, 16, 16, 16, 33, 8, 1, K.Q4_0)"),
+        ("k above 16384", "K.matmul(kern, 0, 16, 16, 16, 16416, 8, 1, K.F32)"),
+        ("zero batch", "K.matmul(kern, 0, 16, 16, 16, 32, 8, 0, K.F32)"),
+        ("null output", "K.matmul(kern, 0, 0, 16, 16, 32, 8, 1, K.F32)"),
+        ("bad tile", "K.matmul(kern, 0, 16, 16, 16, 32, 8, 1, K.F32, tile=4)"),
+        ("i8 without scales", "K.matmul(kern, 0, 16, 16, 16, 32, 8, 1, K.ROWWISE_I8)"),
+        ("q6_k on legacy matmul", "K.matmul(kern, 0, 16, 16, 16, 32, 8, 1, 4)"),
+        ("overflowing n*batch", "K.matmul(kern, 0, 16, 16, 16, 32, 1 << 28, 4, K.F32)"),
+        ("elementwise width", "K.elementwise(kern, 0, 16, 16, 16, 100, 33, 100, K.ADD)"),
+        ("rms epsilon", "K.elementwise(kern, 0, 16, 16, 16, 64, 32, 64, K.RMS_NORM, 0.0)"),
+        ("i8 upload bounds", "K.upload_i8_rows(0, 16, 32, 4, 3, 2, 16)"),
+    ],
+)
+def test_contract_violations_abort(case, call):
+    """src/k200.cpp:271-277 and :283-286: invalid calls abort before any launch."""
+    r = _run_contract(call)
+    assert r.returncode != 0, f"{case}: call was accepted"
+    assert "Kunlun invalid argument" in r.stderr, r.stderr

@@ -1,0 +1,252 @@
+"""GPU parity of kunlun::matmul (called through the C ABI) against the CPU oracle.
+
+Bars (BASELINE north star and bench/library-bench.cpp:125-126):
+  * f32 / f16 / q4_0 weights with f32 activations: the kernels compute in FP32
+    like kernels/kunlun-matvec.xpu; every output must satisfy
+        |y - gold| <= TOL * (1 + |gold|),  TOL = 1e-5,
+    with gold the double-precision sum over the exactly decoded weights
+    (library-bench's gold loop).  That is tighter than the reference's own
+    1e-3 and covers the F16 1e-3 / F32 1e-5 relative bars;
+  * rowwise_i8: bit-exact.  The packed weights, the quantised activations and
+    the outputs (exact int32 dots, then the combine formula of
+    kernels/kunlun-combine.xpu:19) equal the oracle bit for bit.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-5
+
+
+def _device_matmul(K, wtype, wbytes, x, k, n, batch, w_offset=0, x_offset=0):
+    """Upload, run one matmul on device 0, download Y."""
+    wbytes = np.ascontiguousarray(wbytes).view(np.uint8).ravel()
+    dw = K.Buffer(0, wbytes.nbytes + 64)
+    dx = K.Buffer(0, x.nbytes + 64)
+    dy = K.Buffer(0, 4 * n * batch)
+    K.select(0)
+    K.check(K.copy(dw.data() + w_offset, wbytes, wbytes.nbytes, K.HOST_TO_DEVICE))
+    K.check(K.copy(dx.data() + x_offset, np.ascontiguousarray(x, np.float32), x.nbytes, K.HOST_TO_DEVICE))
+    kern = K.Kernel()
+    K.matmul(kern, 0, dy, dw.data() + w_offset, dx.data() + x_offset, k, n, batch, wtype)
+    K.select(0)
+    K.check(K.wait())
+    y = dy.download(np.float32, n * batch)
+    kern.close()
+    return y
+
+
+def _check_float(y, gold, tol=TOL):
+    err = np.abs(y.astype(np.float64) - gold)
+    bound = tol * (1.0 + np.abs(gold))
+    assert np.isfinite(y).all()
+    worst = int(np.argmax(err / bound))
+    assert (err <= bound).all(), f"max err {err[worst]:.3e} at {worst} (gold {gold[worst]:.6f}, bound {bound[worst]:.3e})"
+
+
+def _q4_case(O, k, n, batch, seed=0x7340D123):
+    w = O.normal(seed, n * k, 0.0, 0.02)
+    q4 = O.q4_0_quantize(w, n, k)
+    x = O.uniform(0x09200ABC, k * batch, -1.0, 1.0)
+    return q4, x
+
+
+# ---- q4_0 ---------------------------------------------------------------
+@pytest.mark.parametrize(
+    "k,n,batch",
+    [
+        (4096, 4096, 1),     # config 0
+        (4096, 11008, 1),    # config 1, up projection
+        (11008, 4096, 1),    # config 1, down projection
+        (96, 33, 3),         # odd block count, N tail, a lone third column
+        (32, 1, 1),          # smallest legal shape
+        (8224, 17, 2),       # K % 256 != 0: rows not 16-byte multiples
+        (4096, 300, 9),      # several column groups
+    ],
+)
+def test_q4_0_matches_fp64_gold(K, O, gpu, k, n, batch):
+    q4, x = _q4_case(O, k, n, batch)
+    y = _device_matmul(K, K.Q4_0, q4, x, k, n, batch)
+    gold = O.matmul_gold(q4, O.WT_Q4_0, x, k, n, batch)
+    _check_float(y, gold)
+
+
+def test_q4_0_library_bench_closed_form(K, O, gpu):
+    """bench/library-bench.cpp:89-101 inputs at the verify.sh shape (256, 65, 4)."""
+    k, n, b = 256, 65, 4
+    _, q4 = O.library_bench_weights(k, n)
+    x = O.library_bench_input(k, b)
+    y = _device_matmul(K, K.Q4_0, q4, x, k, n, b)
+    gold = O.matmul_gold(q4, O.WT_Q4_0, x, k, n, b)
+    _check_float(y, gold)
+    # and the reference's own (looser) criterion
+    assert (np.abs(y - gold) <= 1e-3 * (1 + np.abs(gold))).all()
+
+
+def test_q4_0_reference_fixture(K, O, gpu):
+    """native_q4_bench fixtures (random scales incl. zero scales, patterns 0/1/4)."""
+    k, n = 512, 64
+    q4 = O.fixture_q4(k, n)
+    for pattern in (0, 1, 4):
+        x = O.fixture_input(k, 2, pattern)
+        y = _device_matmul(K, K.Q4_0, q4, x, k, n, 2)
+        gold = O.matmul_gold(q4, O.WT_Q4_0, x, k, n, 2)
+        _check_float(y, gold)
+
+
+def test_q4_0_unaligned_pointers(K, O, gpu):
+    """Weights at a 2-byte offset and X at a 4-byte offset take the generic path."""
+    k, n, b = 4096, 40, 2
+    q4, x = _q4_case(O, k, n, b)
+    y = _device_matmul(K, K.Q4_0, q4, x, k, n, b, w_offset=2, x_offset=4)
+    gold = O.matmul_gold(q4, O.WT_Q4_0, x, k, n, b)
+    _check_float(y, gold)
+
+
+def test_q4_0_bitwise_reproducible(K, O, gpu):
+    k, n = 4096, 4096
+    q4, x = _q4_case(O, k, n, 1)
+    y1 = _device_matmul(K, K.Q4_0, q4, x, k, n, 1)
+    y2 = _device_matmul(K, K.Q4_0, q4, x, k, n, 1)
+    assert np.array_equal(y1.view(np.uint32), y2.view(np.uint32))
+
+
+# ---- f16 / f32 ----------------------------------------------------------------
+@pytest.mark.parametrize("wtype", ["f16", "f32"])
+@pytest.mark.parametrize("k,n,batch", [(8192, 8193, 1), (8192, 1024, 2), (96, 33, 2), (256, 65, 4), (32, 5, 3)])
+def test_dense_matches_fp64_gold(K, O, gpu, wtype, k, n, batch):
+    w = O.uniform(0x7340D123, n * k, -1.0, 1.0)
+    x = O.uniform(0x09200ABC, k * batch, -1.0, 1.0)
+    if wtype == "f16":
+        wb = O.f16(w)
+        t = K.F16
+        gold = O.matmul_gold(wb, O.WT_F16, x, k, n, batch)
+    else:
+        wb = w
+        t = K.F32
+        gold = O.matmul_gold(wb, O.WT_F32, x, k, n, batch)
+    y = _device_matmul(K, t, wb, x, k, n, batch)
+    _check_float(y, gold)
+    if wtype == "f16":
+        # north-star bar against the unrounded f32 weights: max relative error <= 1e-3
+        g32 = O.matmul_gold(w, O.WT_F32, x, k, n, batch)
+        rel = np.abs(y - g32) / np.maximum(np.abs(g32), 1.0)
+        assert rel.max() <= 1e-3
+
+
+def test_f16_batch64_column_groups(K, O, gpu):
+    """Config 3 at batch 64 on a reduced N (the batched path covers all columns)."""
+    k, n, b = 8192, 256, 64
+    w = O.f16(O.uniform(1, n * k, -1.0, 1.0))
+    x = O.uniform(2, k * b, -1.0, 1.0)
+    y = _device_matmul(K, K.F16, w, x, k, n, b)
+    _check_float(y, O.matmul_gold(w, O.WT_F16, x, k, n, b))
+
+
+# ---- rowwise int8 ------------------------------------------------------------
+def _i8_case(K, O, k, n, batch, seed=0x7340D123):
+    w = O.normal(seed, n * k, 0.0, 0.02)
+    x = O.normal(0x09200ABC, k * batch, 0.0, 1.0)
+    size = K.packed_i8_size(k, n)
+    dw = K.Buffer(0, size)
+    K.upload_i8_rows(0, dw, k, n, 0, n, w)
+    dx = K.Buffer(0, x.nbytes)
+    dx.upload(x)
+    dy = K.Buffer(0, 4 * n * batch)
+    kern = K.Kernel()
+    K.matmul(kern, 0, dy, dw, dx, k, n, batch, K.ROWWISE_I8,
+             K.packed_i8_scales(dw, k, n), K.packed_i8_maxima(dw, k, n))
+    K.select(0)
+    K.check(K.wait())
+    y = dy.download(np.float32, n * batch)
+    packed = dw.download(np.uint8, size)
+    kern.close()
+    return w, x, y, packed
+
+
+@pytest.mark.parametrize("k,n,batch", [(256, 65, 4), (8192, 1024, 1), (8192, 512, 32), (4096, 300, 9), (32, 3, 1)])
+def test_rowwise_i8_bit_exact(K, O, gpu, k, n, batch):
+    w, x, y, packed = _i8_case(K, O, k, n, batch)
+    wq, scales = O.i8_pack_rows(w, k, n)
+    # packed layout of src/k200.cpp:98-101 (int8 rows | scales | maxima)
+    assert np.array_equal(packed[: k * n].view(np.int8), wq)
+    off = O.aligned(k * n)
+    assert np.array_equal(packed[off: off + 4 * n].view(np.float32).view(np.uint32), scales.view(np.uint32))
+    moff = off + O.aligned(4 * n)
+    assert np.array_equal(packed[moff: moff + 24].view(np.float32), np.full(6, 127.0, np.float32))
+    q0, q1, m0, m1 = O.a8_tensor(x)
+    expect = O.i8_matmul(wq, scales, q0, q1, m0, m1, k, n, batch)
+    assert np.array_equal(y.view(np.uint32), expect.view(np.uint32))
+    # the reference's own tolerance against the f32 gold (library-bench: 2e-2)
+    gold = O.matmul_gold(w, O.WT_F32, x, k, n, batch)
+    assert (np.abs(y - gold) <= 2e-2 * (1 + np.abs(gold))).all()
+
+
+def test_rowwise_i8_zero_activation(K, O, gpu):
+    """max0 == 0 falls back to 1 (src/k200.cpp:214); zero rows keep scale 1."""
+    k, n = 64, 8
+    w = O.normal(5, n * k, 0.0, 0.02)
+    w[:k] = 0.0
+    size = K.packed_i8_size(k, n)
+    dw = K.Buffer(0, size)
+    K.upload_i8_rows(0, dw, k, n, 0, n, w)
+    dx = K.Buffer(0, 4 * k)
+    dx.upload(np.zeros(k, np.float32))
+    dy = K.Buffer(0, 4 * n)
+    kern = K.Kernel()
+    K.matmul(kern, 0, dy, dw, dx, k, n, 1, K.ROWWISE_I8, K.packed_i8_scales(dw, k, n), K.packed_i8_maxima(dw, k, n))
+    K.select(0)
+    K.check(K.wait())
+    y = dy.download(np.float32, n)
+    assert (y == 0).all()
+    scales = dw.download(np.float32, n, O.aligned(k * n))
+    assert scales[0] == 1.0
+
+
+def test_i8_partial_row_upload(K, O, gpu):
+    """upload_i8_rows(first_row, count) fills only its rows (src/k200.cpp:119-120)."""
+    k, n = 128, 10
+    w = O.normal(9, n * k, 0.0, 0.02)
+    size = K.packed_i8_size(k, n)
+    dw = K.Buffer(0, size)
+    K.upload_i8_rows(0, dw, k, n, 0, 4, w[: 4 * k])
+    K.upload_i8_rows(0, dw, k, n, 4, 6, w[4 * k:])
+    packed = dw.download(np.uint8, size)
+    wq, scales = O.i8_pack_rows(w, k, n)
+    assert np.array_equal(packed[: k * n].view(np.int8), wq)
+    off = O.aligned(k * n)
+    assert np.array_equal(packed[off: off + 4 * n].view(np.float32), scales)
+
+
+# ---- elementwise (library-bench `pipeline` and elementwise ops) ----------------
+@pytest.mark.parametrize("op", ["add", "multiply", "silu", "rms", "scale"])
+def test_elementwise_library_bench(K, O, gpu, op):
+    """bench/library-bench.cpp:150-179 at its defaults (K=256, batch=4)."""
+    k, b = 256, 4
+    count = k * b
+    a = np.sin(np.arange(count, dtype=np.float32) * np.float32(0.021)).astype(np.float32)
+    bb = np.cos(np.arange(k, dtype=np.float32) * np.float32(0.04)).astype(np.float32)
+    parameter = 0.75 if op == "scale" else 1e-5
+    a2 = a.reshape(b, k).astype(np.float64)
+    if op == "add":
+        gold = a2 + bb
+    elif op == "multiply":
+        gold = a2 * bb
+    elif op == "silu":
+        gold = a2 / (1 + np.exp(-a2))
+    elif op == "scale":
+        gold = a2 * parameter
+    else:
+        gold = a2 / np.sqrt((a2 * a2).sum(1, keepdims=True) / k + parameter)
+    da, db, dy = K.Buffer(0, 4 * count), K.Buffer(0, 4 * k), K.Buffer(0, 4 * count)
+    da.upload(a)
+    db.upload(bb)
+    kern = K.Kernel()
+    opcode = {"add": K.ADD, "multiply": K.MULTIPLY, "silu": K.SILU, "rms": K.RMS_NORM, "scale": K.SCALE}[op]
+    out = da if op == "rms" else dy  # rms also exercises the in-place path
+    K.elementwise(kern, 0, out, da, db, count, k, k, opcode, parameter)
+    y = out.download(np.float32, count)
+    assert np.abs(y - gold.ravel()).max() < 1e-4
