@@ -75,6 +75,13 @@ void *k200_stream(int device);
  * CUDA graph; calls that grow scratch (the first rowwise_i8 matmul of a new
  * size) synchronise and must not run during a capture. */
 void k200_set_stream(int device, void *stream);
+/* Declare that on `device` no kernel immediately preceding a matmul on the
+ * library stream writes that matmul's weights (true for inference with
+ * resident weights).  Matmul kernels then stream their first weight chunks
+ * while the preceding kernel is still finishing (programmatic dependent
+ * launch); activations and outputs are still touched only after it
+ * completes.  Default off; KUNLUN_STATIC_WEIGHTS=1 turns it on at start-up. */
+void k200_set_static_weights(int device, int enabled);
 /* Asynchronous copy on the library stream of the current device (pinned host
  * memory makes it truly asynchronous); completion via k200_wait(). */
 int k200_copy_async(void *dst, const void *src, size_t bytes, int kind);

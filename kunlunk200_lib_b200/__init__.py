@@ -60,6 +60,7 @@ _SIGNATURES = {
     "k200_peer_bytes": (C.c_size_t, []),
     "k200_stream": (C.c_void_p, [C.c_int]),
     "k200_set_stream": (None, [C.c_int, C.c_void_p]),
+    "k200_set_static_weights": (None, [C.c_int, C.c_int]),
     "k200_quantize_q4_0": (None, [C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int]),
 }
 
@@ -161,6 +162,11 @@ def stream(device: int) -> int:
 def set_stream(device: int, stream_handle: int | None) -> None:
     """Issue library work of `device` on a caller stream (None: the library's own)."""
     lib().k200_set_stream(device, stream_handle or None)
+
+
+def set_static_weights(device: int, enabled: bool) -> None:
+    """Weights of `device`'s matmuls are never written by the kernel just before them."""
+    lib().k200_set_static_weights(device, 1 if enabled else 0)
 
 
 class runtime_lock:

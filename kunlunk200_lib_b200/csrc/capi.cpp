@@ -10,6 +10,7 @@
 namespace k200 {
 cudaStream_t library_stream(int device);
 void set_stream(int device, cudaStream_t s);
+void set_static_weights(int device, bool on);
 const DeviceInfo &device_info(int device);
 int current_device();
 size_t matmul_count(int device);
@@ -74,6 +75,8 @@ size_t k200_peer_bytes(void) { return k200::peer_byte_count(); }
 void *k200_stream(int device) { return static_cast<void *>(k200::library_stream(device)); }
 
 void k200_set_stream(int device, void *stream) { k200::set_stream(device, static_cast<cudaStream_t>(stream)); }
+
+void k200_set_static_weights(int device, int enabled) { k200::set_static_weights(device, enabled != 0); }
 
 int k200_copy_async(void *dst, const void *src, size_t bytes, int kind) {
     std::lock_guard<std::recursive_mutex> lock(kunlun::runtime_mutex());

@@ -102,12 +102,33 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 __device__ __forceinline__ void pdl_wait_prior() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // Packed f32x2 arithmetic (sm_100a): one instruction, two IEEE f32 results.
-__device__ __forceinline__ unsigned long long f2_pack(float lo, float hi) {
-    return (static_cast<unsigned long long>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
+// Pairs are formed and split with PTX vector moves, which the register
+// allocator resolves to an aligned register pair (no instructions).
+__device__ __forceinline__ unsigned long long u2_pack(uint32_t lo, uint32_t hi) {
+    unsigned long long v;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "r"(lo), "r"(hi));
+    return v;
 }
-__device__ __forceinline__ float f2_lo(unsigned long long v) { return __uint_as_float(static_cast<uint32_t>(v)); }
+__device__ __forceinline__ unsigned long long f2_pack(float lo, float hi) {
+    return u2_pack(__float_as_uint(lo), __float_as_uint(hi));
+}
+__device__ __forceinline__ float f2_lo(unsigned long long v) {
+    uint32_t lo, hi;
+    asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(v));
+    (void)hi;
+    return __uint_as_float(lo);
+}
 __device__ __forceinline__ float f2_hi(unsigned long long v) {
-    return __uint_as_float(static_cast<uint32_t>(v >> 32));
+    uint32_t lo, hi;
+    asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(v));
+    (void)lo;
+    return __uint_as_float(hi);
+}
+// lo + hi of a pair
+__device__ __forceinline__ float f2_sum(unsigned long long v) {
+    uint32_t lo, hi;
+    asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(v));
+    return __uint_as_float(lo) + __uint_as_float(hi);
 }
 __device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b,
                                                      unsigned long long c) {

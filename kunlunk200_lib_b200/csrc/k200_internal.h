@@ -26,6 +26,8 @@ struct GemvRequest {
     int k, n, batch;
     int x_stride, q_stride, y_stride;
     long long q_comp;              // elements between component 0 and 1 of q (wt 3)
+    bool prefetch_weights;         // weights are not written by the preceding kernel: stream
+                                   // them before that kernel completes (programmatic launch)
 };
 
 // Streaming GEMV launcher (handles any batch by column groups).

@@ -45,6 +45,7 @@ struct DeviceState {
     k200::DeviceInfo info;
     std::atomic<size_t> allocated{0};
     std::atomic<size_t> matmuls{0};
+    bool static_weights = false;     // see k200_set_static_weights
 };
 DeviceState devices[kMaxDevices];
 
@@ -96,6 +97,8 @@ DeviceState &state(int id) {
                   "cudaHostGetDevicePointer");
         d.info.id = id;
         d.info.err = dev_err;
+        const char *sw = std::getenv("KUNLUN_STATIC_WEIGHTS");
+        d.static_weights = sw && std::strcmp(sw, "1") == 0;
         fail_cuda(cudaDeviceGetAttribute(&d.info.sm_count, cudaDevAttrMultiProcessorCount, id), "sm count");
         fail_cuda(cudaDeviceGetAttribute(&d.info.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, id),
                   "smem opt-in");
@@ -309,6 +312,7 @@ void matmul(Kernel &kernel, int id, void *y, const void *w, const void *x, int k
     r.batch = batch;
     r.x_stride = k;
     r.y_stride = n;
+    r.prefetch_weights = d.static_weights;
     if (type == WeightType::rowwise_i8) {
         const size_t count = (size_t)k * batch;
         grow(s, s.quant, s.quant_size, aligned(2 * count));
@@ -399,6 +403,11 @@ cudaStream_t library_stream(int device) {
     kunlun::require(device >= 0 && device < kunlun::cuda_device_count());
     std::lock_guard<std::recursive_mutex> lock(kunlun::mutex);
     return kunlun::state(device).stream;
+}
+void set_static_weights(int device, bool on) {
+    kunlun::require(device >= 0 && device < kunlun::cuda_device_count());
+    std::lock_guard<std::recursive_mutex> lock(kunlun::mutex);
+    kunlun::state(device).static_weights = on;
 }
 void set_stream(int device, cudaStream_t s) {
     kunlun::require(device >= 0 && device < kunlun::cuda_device_count());
