@@ -93,6 +93,32 @@ void k200_quantize_q4_0(int device, void *q4, const float *w, int k, int n);
 void k200_pack_i8_rows_device(int device, void *weights, int k, int rows, int first_row, int count,
                               const float *device_input);
 
+/* Rowwise-int8 matmul that allocates nothing.  No counterpart in the
+ * reference: kunlun::matmul keeps the quantised activations in scratch owned
+ * by the Kernel and grows it with cudaMalloc/cudaFree (after a full
+ * synchronisation) whenever batch*k grows.  Callers that cannot allocate at
+ * call time -- those that have handed all free device memory to their own
+ * pool, or that cannot afford the device-wide synchronisation cudaFree
+ * implies in the middle of a serving loop -- use this instead.  The scratch is
+ * one fixed array per device in the library's device image, so:
+ *   - batch*k must be <= K200_NOALLOC_MAX_ELEMENTS; larger calls return
+ *     K200_NOALLOC_TOO_LARGE (with a message on stderr) and do nothing;
+ *   - the device must already be set up by k200_select(device) (which creates
+ *     its stream and error word), else K200_NOALLOC_NOT_READY;
+ *   - overlapping calls on one device race on that array: calls issued on the
+ *     same stream are ordered, but calls whose work can run concurrently
+ *     (issued on different streams, see k200_set_stream) are not, and must be
+ *     serialised by the caller.  (Each process has its own copy.)
+ * Arguments, packing and results are those of k200_matmul with type 3
+ * (rowwise_i8); results are bit-identical.  Returns 0 once the work is
+ * submitted (completion via k200_select + k200_wait), a K200_NOALLOC_* status,
+ * or a CUDA error code.  Contract violations abort as in k200_matmul. */
+#define K200_NOALLOC_MAX_ELEMENTS 2097152
+#define K200_NOALLOC_TOO_LARGE (-2)
+#define K200_NOALLOC_NOT_READY (-3)
+int k200_matmul_i8_noalloc(int device, void *y, const void *w, const void *x, int k, int n, int batch,
+                           const float *scales, const float *maxima);
+
 #ifdef __cplusplus
 }
 #endif

@@ -62,6 +62,8 @@ _SIGNATURES = {
     "k200_set_stream": (None, [C.c_int, C.c_void_p]),
     "k200_set_static_weights": (None, [C.c_int, C.c_int]),
     "k200_quantize_q4_0": (None, [C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int]),
+    "k200_matmul_i8_noalloc": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
+                                         C.c_void_p, C.c_void_p]),
 }
 
 
@@ -287,6 +289,19 @@ def elementwise(kernel: Kernel, device: int, y, a, b, count: int, width: int, b_
 def quantize_q4_0(device: int, q4, w, k: int, n: int) -> None:
     """GGML Q4_0 block quantiser on the device (f32 [n][k] -> [n][k/32] blocks)."""
     lib().k200_quantize_q4_0(device, _ptr(q4), _ptr(w), k, n)
+
+
+NOALLOC_MAX_ELEMENTS, NOALLOC_TOO_LARGE, NOALLOC_NOT_READY = 2097152, -2, -3
+
+
+def matmul_i8_noalloc(device: int, y, w, x, k: int, n: int, batch: int, scales, maxima) -> int:
+    """Rowwise-int8 matmul on the library's static scratch (no allocation; see k200_c.h).
+
+    Returns 0 once submitted, NOALLOC_TOO_LARGE when batch*k > NOALLOC_MAX_ELEMENTS,
+    NOALLOC_NOT_READY before the first select(device), else a CUDA error code.
+    """
+    return lib().k200_matmul_i8_noalloc(device, _ptr(y), _ptr(w), _ptr(x), k, n, batch, _ptr(scales),
+                                        _ptr(maxima))
 
 
 def matmul_count(device: int) -> int:

@@ -110,4 +110,12 @@ void k200_pack_i8_rows_device(int device, void *weights, int k, int rows, int fi
                                        cudaMemcpyHostToDevice, s));
 }
 
+int k200_matmul_i8_noalloc(int device, void *y, const void *w, const void *x, int k, int n, int batch,
+                           const float *scales, const float *maxima) {
+    static_assert(K200_NOALLOC_MAX_ELEMENTS == k200::kNoAllocMaxElements, "k200_c.h limit out of date");
+    static_assert(K200_NOALLOC_TOO_LARGE == k200::kNoAllocTooLarge, "k200_c.h status out of date");
+    static_assert(K200_NOALLOC_NOT_READY == k200::kNoAllocNotReady, "k200_c.h status out of date");
+    return k200::matmul_i8_noalloc(device, y, w, x, k, n, batch, scales, maxima);
+}
+
 }  // extern "C"

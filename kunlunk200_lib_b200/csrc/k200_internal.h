@@ -53,4 +53,18 @@ cudaError_t launch_elementwise(float *y, const float *a, const float *b, int n, 
 // GGML Q4_0 block quantiser (f32 [n][k] -> 18-byte blocks).
 cudaError_t launch_q4_0_quantize(const float *w, int n, int k, uint8_t *q4, cudaStream_t stream);
 
+// Static scratch of the allocation-free rowwise-int8 matmul (static_scratch.cu):
+// room for batch*k <= kNoAllocMaxElements activations, two int8 components
+// each, plus a 256-byte parameter block.
+constexpr size_t kNoAllocMaxElements = size_t(1) << 21;
+constexpr size_t kNoAllocParamsOffset = 2 * kNoAllocMaxElements;
+constexpr size_t kNoAllocScratchBytes = kNoAllocParamsOffset + 256;
+// Device address of that scratch on the CURRENT device (cudaGetSymbolAddress).
+cudaError_t noalloc_scratch_address(void **ptr);
+// Statuses of matmul_i8_noalloc besides CUDA errors (K200_NOALLOC_* in k200_c.h).
+constexpr int kNoAllocTooLarge = -2;
+constexpr int kNoAllocNotReady = -3;
+int matmul_i8_noalloc(int device, void *y, const void *w, const void *x, int k, int n, int batch,
+                      const float *scales, const float *maximum);
+
 }  // namespace k200

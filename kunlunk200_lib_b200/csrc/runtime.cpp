@@ -46,6 +46,7 @@ struct DeviceState {
     std::atomic<size_t> allocated{0};
     std::atomic<size_t> matmuls{0};
     bool static_weights = false;     // see k200_set_static_weights
+    void *noalloc_scratch = nullptr; // static scratch address (k200_matmul_i8_noalloc)
 };
 DeviceState devices[kMaxDevices];
 
@@ -426,4 +427,76 @@ size_t matmul_count(int device) {
 }
 size_t peer_copy_count() { return kunlun::peer_copies.load(); }
 size_t peer_byte_count() { return kunlun::peer_bytes.load(); }
+
+// Rowwise-int8 matmul whose activation scratch is the module's static array
+// instead of the Kernel's grown buffer.  Same contract, kernels and results as
+// kunlun::matmul(..., rowwise_i8, ...).  Nothing here allocates: the size
+// check comes before any CUDA call, the device must already be set up (its
+// stream and error word are created by the first select), and the scratch
+// address is looked up once per device.
+int matmul_i8_noalloc(int id, void *y, const void *w, const void *x, int k, int n, int batch, const float *scales,
+                      const float *maximum) {
+    using namespace kunlun;
+    if (k > 0 && batch > 0 && (size_t)k * (size_t)batch > kNoAllocMaxElements) {
+        std::fprintf(stderr,
+                     "k200_matmul_i8_noalloc: batch*k = %zu exceeds the static scratch limit of %zu elements "
+                     "(use k200_matmul)\n",
+                     (size_t)k * (size_t)batch, kNoAllocMaxElements);
+        std::fflush(stderr);
+        return kNoAllocTooLarge;
+    }
+    std::lock_guard<std::recursive_mutex> lock(mutex);
+    require(id >= 0 && id < cuda_device_count());
+    require(k > 0 && k <= 16384 && k % 32 == 0 && n > 0 && batch > 0 && n <= INT_MAX / batch);
+    require((size_t)n * batch <= INT_MAX / 4 && (size_t)n <= INT_MAX / (size_t)k);
+    require(y && w && x && scales && maximum);
+    DeviceState &d = devices[id];
+    if (!d.ready) {
+        std::fprintf(stderr, "k200_matmul_i8_noalloc: device %d is not set up; call k200_select(%d) once first\n",
+                     id, id);
+        std::fflush(stderr);
+        return kNoAllocNotReady;
+    }
+    kunlun::select(id);  // the state exists, so this only makes the device current
+    if (!d.noalloc_scratch) {
+        void *p = nullptr;
+        cudaError_t e = noalloc_scratch_address(&p);
+        if (e != cudaSuccess || !p) {
+            cudaGetLastError();
+            std::fprintf(stderr, "k200_matmul_i8_noalloc: cudaGetSymbolAddress failed on device %d: %s\n", id,
+                         cudaGetErrorString(e));
+            std::fflush(stderr);
+            return e != cudaSuccess ? (int)e : (int)cudaErrorInvalidSymbol;
+        }
+        d.noalloc_scratch = p;
+    }
+    const size_t count = (size_t)k * batch;
+    int8_t *q = static_cast<int8_t *>(d.noalloc_scratch);
+    float *maxima = reinterpret_cast<float *>(static_cast<char *>(d.noalloc_scratch) + kNoAllocParamsOffset);
+    void *words = static_cast<char *>(d.noalloc_scratch) + kNoAllocParamsOffset + 64;
+    // launch_a8_tensor zeroes the reduction words itself before the
+    // multi-CTA passes (cudaMemsetAsync, no allocation); the single-CTA form
+    // writes every word it reads.
+    cudaError_t e = launch_a8_tensor(static_cast<const float *>(x), count, q, maxima, words, d.info, d.stream);
+    if (e != cudaSuccess) return (int)e;
+    GemvRequest r{};
+    r.wt = (int)WeightType::rowwise_i8;
+    r.w = w;
+    r.y = static_cast<float *>(y);
+    r.k = k;
+    r.n = n;
+    r.batch = batch;
+    r.x_stride = k;
+    r.y_stride = n;
+    r.q = q;
+    r.q_stride = k;
+    r.q_comp = (long long)count;
+    r.act_max = maxima;
+    r.row_scale = scales;
+    r.prefetch_weights = d.static_weights;
+    e = launch_gemv(r, d.info, d.stream);
+    if (e != cudaSuccess) return (int)e;
+    ++d.matmuls;
+    return 0;
+}
 }  // namespace k200
