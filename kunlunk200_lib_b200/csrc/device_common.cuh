@@ -18,9 +18,8 @@ enum KernelError : int {
     kErrPeerTimeout = 0x4b03,   // a peer flag never arrived
 };
 
-// Budget for one mbarrier wait: try_wait suspends for a hardware-defined
-// interval per attempt, so this is on the order of seconds in total.
-constexpr uint32_t kWaitBudget = 1u << 22;
+// Budget for one mbarrier wait, in try_wait attempts.
+constexpr uint32_t kWaitBudget = 1u << 19;
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -47,20 +46,24 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// One potentially blocking test of an mbarrier phase: a thread whose phase
+// is not complete is suspended until it completes or about kSuspendNs pass,
+// so waiting warps do not take issue slots from working ones.
+constexpr uint32_t kSuspendNs = 2000;
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "n"(kSuspendNs)
         : "memory");
     return ok != 0;
 }
 
 // Bounded wait on an mbarrier phase.  Returns false (and posts `code`) when
-// the budget runs out.
+// the budget runs out (at most kWaitBudget suspensions, about a second).
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
     for (uint32_t i = 0; i < kWaitBudget; ++i)
         if (mbar_try_wait(bar, parity)) return true;

@@ -1,0 +1,717 @@
+// Q4_0 matrix-vector product for one activation column on the tensor cores
+// (sm_100a): Y[r] = sum_b d[r,b] * sum_j (q[r,b,j] - 8) * x[32b + j], the
+// arithmetic of kernels/kunlun-matvec.xpu:37-77 of the reference.
+//
+// Why this kernel exists: at batch 1 a Q4_0 GEMV is bounded by how fast the
+// SMs can turn nibbles into numbers, not by HBM, unless the decode costs
+// about one instruction per weight.  Here two nibbles become two exact f16
+// values (v - 8) with one LOP3 (OR the nibble into the mantissa of 1024.0)
+// plus one HADD2/HFMA2, and mma.sync m16n8k16 does the multiply-add.  The
+// activations are split into f16 hi + lo halves (x = hi + lo to about 22
+// bits) after a power-of-two scaling per 32-element block, the fp16 block
+// scale d is applied in f32 to each block's dot product, and partial sums
+// are f32.  Results agree with the reference's FP32 arithmetic to within its
+// rounding (the products (v-8)*hi and (v-8)*lo are exact; the error is the
+// hi/lo truncation, about 2^-22 relative per term, plus f32 summation).
+//
+// Layout and work split:
+//  * the unit of work is a "pair": 32 rows x 144 bytes of the weight matrix
+//    (eight Q4_0 blocks of each row, two "groups" of four blocks).  Pairs
+//    are numbered row-tile-major and every CTA (one per SM) takes a
+//    contiguous range of them, so the bytes per CTA are balanced to within
+//    one pair;
+//  * a producer thread streams the CTA's range through a ring of stages with
+//    2-D TMA tensor copies (cp.async.bulk.tensor + mbarriers) of boxes up to
+//    seven pairs wide (32 rows x 1008 bytes), using 5-, 3- and 1-pair boxes
+//    at the ends of a row tile or of the range.  Measured on B200: boxes
+//    with 144-byte rows stream at ~2 TB/s (the copy engine's cost is per
+//    box row), 432-1008-byte rows at 5.3-6.2 TB/s.  Odd widths keep the
+//    shared-memory row pitch (36*w words) conflict-free for the lane pattern
+//    below;
+//  * consumer warp w processes pairs w, w + 16, ... of the range.  A stage
+//    holds one box; before waiting on a stage's mbarrier a warp checks the
+//    box sequence number the producer stored for the stage (a warp may run
+//    several boxes ahead, and an mbarrier parity alone only tells adjacent
+//    phases apart), and the last warp to finish a box's pairs releases it;
+//  * within a pair a warp computes two m16 tiles (rows 0-15 and 16-31) per
+//    group.  For group q the four blocks use the four column pairs of the
+//    n8 MMA: column pair i holds (hi, lo) of block beta(i)'s activations and
+//    zero elsewhere, so after the 8 MMAs of a group the accumulator holds
+//    four separate block dots and lane c of each quad finds block beta(c)
+//    in its own columns.  Each lane then applies d and the activation scale
+//    of one block per row and accumulates in f32;
+//  * activations are prepared once per CTA into "fragment records" in shared
+//    memory (544 bytes per group: the B fragments of the four column pairs,
+//    16 zero bytes and the four block scales), so the main loop reads them
+//    with one 16-byte load per block;
+//  * a row tile is finished by the last of the CTA's warps to arrive at it:
+//    it sums the warps' partials in warp order and stores Y, or, for a tile
+//    shared with other CTAs, publishes its sum (if a lower CTA holds the
+//    tile's first pairs) or collects the higher CTAs' published sums in CTA
+//    order before storing Y, so results do not depend on timing.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+
+#include "device_common.cuh"
+#include "k200_internal.h"
+
+namespace k200 {
+
+namespace {
+
+constexpr int kTileRows = 32;
+constexpr int kPairBytes = 144;                        // two groups of four blocks
+constexpr int kPairWords = kPairBytes / 4;
+constexpr int kGroupBytes = 72;
+constexpr int kMaxBoxPairs = 7;                        // widest box: 32 rows x 1008 bytes
+constexpr int kStageBytes = kTileRows * kPairBytes * kMaxBoxPairs;  // 32256
+constexpr int kMaxStages = 8;
+constexpr int kRecBytes = 544;                         // fragment record of one group
+constexpr int kZeroOff = 512, kScaleOff = 528;
+constexpr int kWarps = 16;                             // consumer warps
+constexpr int kThreads = (kWarps + 1) * 32;
+
+struct Q4MmaArgs {
+    const float *x;
+    float *y;
+    unsigned long long *slot;  // [grid][32] tagged partial sums of row tiles shared with other CTAs
+    int *err;
+    long long units;    // row tiles * pairs per row
+    int k, n, tiles, ppr, grid, prefetch;
+    int max_tiles;      // row tiles any CTA touches (partial-sum slots in shared memory)
+    int stages;         // ring stages (<= kMaxStages)
+    int max_pairs;      // pairs any CTA processes (box tables in shared memory)
+};
+
+// Tensor maps over the weight rows viewed as 32-bit words [n][row_bytes/4],
+// with boxes of 32 rows x 7, 5, 3 and 1 pairs.
+struct Q4MmaMaps {
+    CUtensorMap box[4];
+};
+__host__ __device__ constexpr int map_of_width(int w) { return (kMaxBoxPairs - w) / 2; }
+
+// The CTA's pairs [u, end) covered by boxes: as wide as possible (7 pairs),
+// never across a row tile, odd widths only.  Producer and consumers walk the
+// same sequence.
+struct BoxWalk {
+    long long u, end;
+    int tile, pair, width, ppr;
+    __device__ BoxWalk(long long begin, long long end_, int ppr_) : u(begin), end(end_), ppr(ppr_) {
+        tile = static_cast<int>(begin / ppr);
+        pair = static_cast<int>(begin - static_cast<long long>(tile) * ppr);
+        fit();
+    }
+    __device__ void fit() {
+        const long long left = min(static_cast<long long>(ppr - pair), end - u);
+        width = left >= 7 ? 7 : left >= 5 ? 5 : left >= 3 ? 3 : 1;
+    }
+    __device__ void next() {
+        u += width;
+        pair += width;
+        if (pair == ppr) { pair = 0; ++tile; }
+        fit();
+    }
+};
+
+// Column pair c of the MMA carries block beta(c) of a group, beta = (3, 1, 2, 0),
+// and lane c of a quad finishes that block; beta_inv is the inverse.
+__host__ __device__ constexpr int beta_inv(int b) { return b == 0 ? 3 : b == 1 ? 1 : b == 2 ? 2 : 0; }
+
+// Bytes (qs indices 0..15) of block position p (0..3 in its group) that
+// lane c of a quad decodes.  Groups are 72 bytes (18 words) and start
+// 8-byte aligned; blocks 1 and 3 have their 16 nibble bytes on word
+// boundaries, blocks 0 and 2 are offset by two bytes, so three lanes take
+// aligned words and the fourth combines the two-byte ends of the block.
+__host__ __device__ constexpr void lane_bytes(int p, int c, int (&q)[4]) {
+    if (p & 1) {
+        for (int i = 0; i < 4; ++i) q[i] = 4 * c + i;
+    } else if (p == 0) {
+        if (c < 3) { for (int i = 0; i < 4; ++i) q[i] = 2 + 4 * c + i; }
+        else { q[0] = 0; q[1] = 1; q[2] = 14; q[3] = 15; }
+    } else {
+        if (c == 0) { q[0] = 0; q[1] = 1; q[2] = 14; q[3] = 15; }
+        else { for (int i = 0; i < 4; ++i) q[i] = 4 * c - 2 + i; }
+    }
+}
+
+// Lane c's bytes of block position p come in two adjacent pairs starting at
+// pair_first and pair_second (the activation loader reads them as float2s).
+__host__ __device__ constexpr int pair_first(int p, int c) {
+    return (p & 1) ? 4 * c : p == 0 ? (c < 3 ? 2 + 4 * c : 0) : (c == 0 ? 0 : 4 * c - 2);
+}
+__host__ __device__ constexpr int pair_second(int p, int c) {
+    return (p & 1) ? 4 * c + 2 : p == 0 ? (c < 3 ? 4 + 4 * c : 14) : (c == 0 ? 14 : 4 * c);
+}
+constexpr bool pairs_match_lane_bytes() {
+    for (int p = 0; p < 4; ++p)
+        for (int c = 0; c < 4; ++c) {
+            int q[4] = {0, 0, 0, 0};
+            lane_bytes(p, c, q);
+            const int a0 = pair_first(p, c), a1 = pair_second(p, c);
+            if (q[0] != a0 || q[1] != a0 + 1 || q[2] != a1 || q[3] != a1 + 1) return false;
+        }
+    return true;
+}
+static_assert(pairs_match_lane_bytes(), "activation pairs disagree with the lane byte map");
+
+template <uint32_t MASK>
+__device__ __forceinline__ uint32_t and_or(uint32_t w, uint32_t m) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(w), "n"(MASK), "r"(m));
+    return d;
+}
+__device__ __forceinline__ uint32_t hadd2_u(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t hfma2_u(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// One 32-bit word of nibble bytes (b0, b1, b2, b3) -> four f16x2 registers of
+// exact (v - 8) values: t0 = {lo(b0), lo(b2)}, t1 = {hi(b0), hi(b2)},
+// t2 = {lo(b1), lo(b3)}, t3 = {hi(b1), hi(b3)}.
+//   lo nibble: (w & 0x000f000f) | 0x6400 pairs = 1024 + v;  + (-1032)      = v - 8
+//   hi nibble: (w & 0x00f000f0) | 0x6400 pairs = 1024 + 16v; * 1/16 + (-72) = v - 8
+__device__ __forceinline__ void decode_word(uint32_t w, uint32_t (&t)[4]) {
+    const uint32_t m = 0x64006400u;
+    const uint32_t w8 = w >> 8;
+    t[0] = hadd2_u(and_or<0x000F000Fu>(w, m), 0xE408E408u);
+    t[1] = hfma2_u(and_or<0x00F000F0u>(w, m), 0x2C002C00u, 0xD480D480u);
+    t[2] = hadd2_u(and_or<0x000F000Fu>(w8, m), 0xE408E408u);
+    t[3] = hfma2_u(and_or<0x00F000F0u>(w8, m), 0x2C002C00u, 0xD480D480u);
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint64_t *bar,
+                                            uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ uint32_t lds(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+template <int OFF>
+__device__ __forceinline__ uint32_t lds_at(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1+%2];" : "=r"(v) : "r"(addr), "n"(OFF));
+    return v;
+}
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ float ldsf(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ void consumer_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(kWarps * 32) : "memory");
+}
+
+// CTA that processes unit u (CTA i owns units [i*U/G, (i+1)*U/G)).
+__device__ __forceinline__ int cta_of(long long u, long long units, int grid) {
+    return static_cast<int>(((u + 1) * grid - 1) / units);
+}
+
+// One B-fragment slot pair of an activation block is built by the four
+// threads of a quad together (thread c writes the hi and lo slots of lane c).
+// load_slot fetches lane c's eight activations: x[a0], x[a0+1], x[a1],
+// x[a1+1] and the same +16 (see lane_bytes); store_slot scales the block by
+// 2^-e so that its largest magnitude lies in [2^14, 2^15), splits the values
+// into f16 hi + lo and stores them (all 32 lanes of the warp must call it).
+__device__ __forceinline__ void load_slot(const float *xb, int p, int c, float (&v)[8]) {
+    const int a0 = pair_first(p, c), a1 = pair_second(p, c);
+    const float2 l0 = __ldg(reinterpret_cast<const float2 *>(xb + a0));
+    const float2 l1 = __ldg(reinterpret_cast<const float2 *>(xb + a1));
+    const float2 h0 = __ldg(reinterpret_cast<const float2 *>(xb + a0 + 16));
+    const float2 h1 = __ldg(reinterpret_cast<const float2 *>(xb + a1 + 16));
+    // register order = fragment order: {q0, q2}, {q0+16, q2+16}, {q1, q3}, {q1+16, q3+16}
+    v[0] = l0.x; v[1] = l1.x; v[2] = h0.x; v[3] = h1.x;
+    v[4] = l0.y; v[5] = l1.y; v[6] = h0.y; v[7] = h1.y;
+}
+
+__device__ __forceinline__ void store_slot(const float (&v)[8], uint8_t *rec, int p, int c, bool store) {
+    uint32_t mx = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) mx = max(mx, __float_as_uint(v[i]) & 0x7fffffffu);
+    mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    int e = 0;  // x = 2^e * x'
+    const bool finite = mx < 0x7f800000u;
+    if (mx != 0 && finite) {
+        int ex = static_cast<int>(mx >> 23) - 127;                                 // floor(log2(max))
+        if (mx < 0x00800000u) ex = (31 - __clz(static_cast<int>(mx))) - 149;       // subnormal max
+        e = min(max(ex - 14, -126), 113);
+    }
+    const float scale = __uint_as_float(static_cast<uint32_t>(127 - e) << 23);  // 2^-e, a normal float
+    uint32_t hi[4], lo[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float u = __fmul_rn(v[2 * i], scale), w = __fmul_rn(v[2 * i + 1], scale);
+        const __half2 h = __floats2half2_rn(u, w);
+        const float2 hf = __half22float2(h);
+        __half2 l = __floats2half2_rn(__fsub_rn(u, hf.x), __fsub_rn(w, hf.y));
+        if (!finite) {
+            // a non-finite hi keeps its Inf/NaN alone (lo = 0), as v*x would
+            if (!((__float_as_uint(hf.x) & 0x7fffffffu) < 0x7f800000u)) l.x = __ushort_as_half(0);
+            if (!((__float_as_uint(hf.y) & 0x7fffffffu) < 0x7f800000u)) l.y = __ushort_as_half(0);
+        }
+        hi[i] = *reinterpret_cast<const uint32_t *>(&h);
+        lo[i] = *reinterpret_cast<const uint32_t *>(&l);
+    }
+    if (!store) return;
+    const int col = beta_inv(p);  // column pair that carries this block
+    *reinterpret_cast<uint4 *>(rec + col * 128 + c * 16) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4 *>(rec + col * 128 + 64 + c * 16) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    if (c == 0) *reinterpret_cast<float *>(rec + kScaleOff + 4 * col) = __uint_as_float(static_cast<uint32_t>(e + 127) << 23);
+    if (c == 0 && p == 0) *reinterpret_cast<uint4 *>(rec + kZeroOff) = make_uint4(0, 0, 0, 0);
+}
+
+// Partial sums of a row tile shared between CTAs travel as 64-bit words
+// {1, f32 bits}: value and "present" tag in one single-copy-atomic access,
+// so the reader needs no fence.  The reader clears each word after use, so
+// every launch starts from zeros.
+__device__ __forceinline__ unsigned long long ld_relaxed(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_relaxed(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+constexpr unsigned long long kPresent = 1ull << 32;
+constexpr uint32_t kPeerBudget = 1u << 20;   // polls of a partial sum (with 64 ns sleeps)
+
+__global__ void __launch_bounds__(kThreads, 1)
+    q4_mma_gemv_kernel(const __grid_constant__ Q4MmaMaps maps, const Q4MmaArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int groups = a.k >> 7;
+    const int S = a.stages;
+    uint8_t *ring = smem;
+    uint8_t *xrec = ring + S * kStageBytes;
+    float *part = reinterpret_cast<float *>(xrec + groups * kRecBytes);  // [max_tiles][kWarps][32]
+    uint64_t *full = reinterpret_cast<uint64_t *>(part + a.max_tiles * kWarps * 32);
+    uint64_t *empty = full + kMaxStages;
+    uint64_t *tables = empty + kMaxStages;                                       // box tables written
+    volatile int *seqno = reinterpret_cast<volatile int *>(tables + 2);         // box held by each stage
+    int *done = const_cast<int *>(seqno) + kMaxStages;                          // pairs finished per stage
+    int *tcnt = done + kMaxStages;                                               // [max_tiles] warp arrivals
+    uint32_t *boxinfo = reinterpret_cast<uint32_t *>(tcnt + a.max_tiles);      // [boxes] see below
+    uint16_t *pairbox = reinterpret_cast<uint16_t *>(boxinfo + a.max_pairs);   // [pairs] box << 3 | pair in box
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const long long u0 = static_cast<long long>(blockIdx.x) * a.units / a.grid;
+    const long long u1 = static_cast<long long>(blockIdx.x + 1) * a.units / a.grid;
+    const int nu = static_cast<int>(u1 - u0);
+    const int t_first = static_cast<int>(u0 / a.ppr);
+    const int t_last = static_cast<int>((u1 - 1) / a.ppr);
+
+    if (tid < S) {
+        mbar_init(&full[tid], 1);
+        mbar_init(&empty[tid], 1);
+        if (tid == 0) mbar_init(tables, 1);
+        fence_mbar_init();
+        seqno[tid] = -1;
+        done[tid] = 0;
+    }
+    if (tid < a.max_tiles) tcnt[tid] = 0;
+    __syncthreads();
+    pdl_launch_dependents();
+
+    if (warp == kWarps) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+#pragma unroll
+            for (int m = 0; m < 4; ++m)
+                asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.box[m])) : "memory");
+            const uint64_t policy = policy_evict_first();
+            const int early = a.prefetch < S ? a.prefetch : S;
+            const uint32_t ring_u = smem_u32(ring);
+            int j = 0, s = 0, phase = 0;
+            for (BoxWalk bw(u0, u1, a.ppr); bw.u < u1; bw.next(), ++j) {
+                if (j >= S && !mbar_wait(&empty[s], phase ^ 1, a.err, kErrBulkTimeout)) break;
+                if (j == early) pdl_wait_prior();
+                seqno[s] = j;
+                mbar_arrive_expect_tx(&full[s], kTileRows * kPairBytes * bw.width);
+                tma_load_2d(ring_u + s * kStageBytes, &maps.box[map_of_width(bw.width)], bw.pair * kPairWords,
+                            bw.tile * kTileRows, &full[s], policy);
+                if (++s == S) { s = 0; phase ^= 1; }
+            }
+            if (j <= early) pdl_wait_prior();
+            // never exit with a copy still writing into this CTA's shared memory
+            for (int i = j > S ? j - S : 0; i < j; ++i)
+                (void)mbar_wait(&full[i % S], (i / S) & 1, a.err, kErrBulkTimeout);
+        } else if (lane == 1) {
+            // the same box sequence, tabulated for the consumers: boxinfo[j] =
+            // tile offset (bits 16..), pair in row (8..15), width (4..7),
+            // stage (1..3), mbarrier parity (0); pairbox[i] = box << 3 | pair in box
+            int j = 0, st = 0, ph = 0;
+            for (BoxWalk bw(u0, u1, a.ppr); bw.u < u1; bw.next(), ++j) {
+                boxinfo[j] = static_cast<uint32_t>((bw.tile - t_first) << 16 | bw.pair << 8 | bw.width << 4 | st << 1 | ph);
+                for (int q = 0; q < bw.width; ++q) pairbox[bw.u - u0 + q] = static_cast<uint16_t>(j << 3 | q);
+                if (++st == S) { st = 0; ph ^= 1; }
+            }
+            mbar_arrive(tables);  // release: the tables are visible to waiters of this phase
+        }
+        return;
+    }
+
+    // ---------------- consumers ----------------
+    pdl_wait_prior();  // x, y and the partial-sum words may belong to the previous kernel
+    {
+        // fragment records: four threads per activation block; every load of a
+        // thread is issued before the first conversion
+        constexpr int kPasses = 4;  // K <= 16384: at most 2048 slots = 4 passes of 512 threads
+        const int nslots = groups * 16;
+        float xv[kPasses][8];
+#pragma unroll
+        for (int k = 0; k < kPasses; ++k)
+            if (k * kWarps * 32 < nslots) {
+                const int b = min(k * kWarps * 32 + tid, nslots - 1) >> 2;
+                load_slot(a.x + 32 * b, b & 3, lane & 3, xv[k]);
+            }
+#pragma unroll
+        for (int k = 0; k < kPasses; ++k)
+            if (k * kWarps * 32 < nslots) {
+                const int t = k * kWarps * 32 + tid, b = min(t, nslots - 1) >> 2;
+                store_slot(xv[k], xrec + (b >> 2) * kRecBytes, b & 3, lane & 3, t < nslots);
+            }
+    }
+    for (int i = tid; i < a.max_tiles * kWarps * 32; i += kWarps * 32) part[i] = 0.f;
+    consumer_sync();
+    if (!mbar_wait(tables, 0, a.err, kErrBulkTimeout)) return;
+
+    const int g = lane >> 2, c = lane & 3;
+    // The five words lane c loads from each of its rows, as byte offsets in
+    // a 72-byte group: A = 4c+4 (block 0; lane 3: block 1's first word, the
+    // partner of its block-0 ends), B = 4c+20 (block 1), C = 4c+36 (block 2;
+    // lane 0: the word holding block 2's first two nibble bytes), D = 4c+56
+    // (block 3) and E = 52, 16, 36, 0 for lanes 0..3 (the other half of a
+    // split block-0/block-2 word, and the word holding the scale d of the
+    // lane's block beta(c)).  A-D are one base register plus immediates.
+    const uint32_t offE = (c == 0 ? 52u : c == 1 ? 16u : c == 2 ? 36u : 0u) - 4u * c;  // relative to 4c
+    const uint32_t selA = c == 3 ? 0x1076u : 0x3210u;  // lane 3: {w0.b2, w0.b3, w4.b0, w4.b1}
+    const uint32_t selC = c == 0 ? 0x5432u : 0x3210u;  // lane 0: {w9.b2, w9.b3, w13.b0, w13.b1}
+    const uint32_t selD = c >= 2 ? 0x1010u : 0x3232u;  // scale half: lanes 2, 3 low, 0, 1 high
+    // B-fragment offsets inside a record for the MMAs of blocks 0..3
+    uint32_t boff[4];
+#pragma unroll
+    for (int b = 0; b < 4; ++b) boff[b] = (g >> 1) == beta_inv(b) ? (g >> 1) * 128 + (g & 1) * 64 + c * 16 : kZeroOff;
+
+    // A row tile is finished by the last of this CTA's warps to arrive at it
+    // (every warp arrives once per tile of the CTA, with or without pairs in
+    // it).  The finishing warp sums the warps' partials in warp order, then
+    //  * stores Y if this CTA holds all of the tile's pairs;
+    //  * publishes the sum if a lower CTA holds the tile's first pairs (that
+    //    CTA finishes the tile; for this CTA it is always its first tile);
+    //  * otherwise (the tile continues in higher CTAs) adds the sums those
+    //    CTAs published, in CTA order, and stores Y.
+    auto finish_tile = [&](int ts) {
+        const int t = t_first + ts;
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) v += part[(ts * kWarps + w) * 32 + lane];
+        const long long tb = static_cast<long long>(t) * a.ppr, te = tb + a.ppr;
+        const int row = t * kTileRows + lane;
+        if (tb < u0) {
+            st_relaxed(a.slot + static_cast<size_t>(blockIdx.x) * 32 + lane, kPresent | __float_as_uint(v));
+            return;
+        }
+        if (te > u1) {
+            const int last = cta_of(te - 1, a.units, a.grid);
+            for (int j0 = blockIdx.x + 1; j0 <= last; j0 += 4) {
+                unsigned long long wv[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    wv[q] = j0 + q <= last ? ld_relaxed(a.slot + static_cast<size_t>(j0 + q) * 32 + lane) : kPresent;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    if (j0 + q > last) break;
+                    unsigned long long *src = a.slot + static_cast<size_t>(j0 + q) * 32 + lane;
+                    for (uint32_t spin = 0; !(wv[q] & kPresent); ++spin) {
+                        if (spin >= kPeerBudget) {
+                            atomicExch(a.err, kErrPeerTimeout);
+                            break;
+                        }
+                        __nanosleep(64);
+                        wv[q] = ld_relaxed(src);
+                    }
+                    v += __uint_as_float(static_cast<uint32_t>(wv[q]));
+                    st_relaxed(src, 0ull);
+                }
+            }
+        }
+        if (row < a.n) a.y[row] = v;
+    };
+    auto arrive = [&](int ts) {
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) {
+            __threadfence_block();
+            last = atomicAdd(&tcnt[ts], 1) == kWarps - 1;
+            __threadfence_block();
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) finish_tile(ts);
+    };
+
+    const uint32_t ring_u = smem_u32(ring), xrec_u = smem_u32(xrec);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};  // rows g, g+8, g+16, g+24 of the current tile
+    int cur = -1, next_arrival = t_first;
+    auto flush = [&](int t) {
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], 1);
+            acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], 2);
+        }
+        if (c == 0) {
+            float *dst = part + ((t - t_first) * kWarps + warp) * 32;
+#pragma unroll
+            for (int r = 0; r < 4; ++r) dst[g + 8 * r] = acc[r];
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[r] = 0.f;
+        arrive(t - t_first);
+        next_arrival = t + 1;
+    };
+
+    for (int i = warp; i < nu; i += kWarps) {
+        const uint32_t pb = pairbox[i];
+        const int j = static_cast<int>(pb >> 3), q = static_cast<int>(pb & 7);
+        const uint32_t info = boxinfo[j];
+        const int s = (info >> 1) & 7, width = (info >> 4) & 15;
+        const int tile = t_first + static_cast<int>(info >> 16);
+        // wait until the stage holds box j, then for its bytes
+        if (seqno[s] != j) {
+            bool ok = true;
+            for (uint32_t spin = 0; seqno[s] != j; ++spin) {
+                if (spin >= kPeerBudget) { atomicExch(a.err, kErrBulkTimeout); ok = false; break; }
+                __nanosleep(32);
+            }
+            if (!ok) break;
+        }
+        if (!mbar_wait(&full[s], info & 1, a.err, kErrBulkTimeout)) break;
+        if (tile != cur) {
+            if (cur >= 0) flush(cur);
+            for (; next_arrival < tile; ++next_arrival) arrive(next_arrival - t_first);
+            cur = tile;
+        }
+        const uint32_t pitch = kPairBytes * width;
+        // this lane's rows g, g+8, g+16, g+24 of the pair, at byte 4c of each group
+        const uint32_t r0 = ring_u + s * kStageBytes + q * kPairBytes + g * pitch + 4 * c;
+        const uint32_t rows[4] = {r0, r0 + 8 * pitch, r0 + 16 * pitch, r0 + 24 * pitch};
+        const uint32_t recp = xrec_u + (((info >> 8) & 255) + q) * 2 * kRecBytes;
+#pragma unroll
+        for (int grp = 0; grp < 2; ++grp) {
+            const uint32_t rec = recp + grp * kRecBytes;
+            uint32_t wq[4][4], dh[4];  // [row][block] nibble words, scale halves
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const uint32_t ro = rows[r];
+                const uint32_t A = grp ? lds_at<72 + 4>(ro) : lds_at<4>(ro);
+                const uint32_t B = grp ? lds_at<72 + 20>(ro) : lds_at<20>(ro);
+                const uint32_t C = grp ? lds_at<72 + 36>(ro) : lds_at<36>(ro);
+                const uint32_t D = grp ? lds_at<72 + 56>(ro) : lds_at<56>(ro);
+                const uint32_t E = grp ? lds_at<72>(ro + offE) : lds_at<0>(ro + offE);
+                wq[r][0] = __byte_perm(A, E, selA);
+                wq[r][1] = B;
+                wq[r][2] = __byte_perm(C, E, selC);
+                wq[r][3] = D;
+                dh[r] = __byte_perm(E, E, selD);
+            }
+            float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};  // tiles rows 0-15, 16-31
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const uint4 xf = lds128(rec + boff[b]);
+                uint32_t t0[4], t1[4], t2[4], t3[4];
+                decode_word(wq[0][b], t0);
+                decode_word(wq[1][b], t1);
+                decode_word(wq[2][b], t2);
+                decode_word(wq[3][b], t3);
+                mma16816(d0, t0[0], t1[0], t0[1], t1[1], xf.x, xf.y);
+                mma16816(d1, t2[0], t3[0], t2[1], t3[1], xf.x, xf.y);
+                mma16816(d0, t0[2], t1[2], t0[3], t1[3], xf.z, xf.w);
+                mma16816(d1, t2[2], t3[2], t2[3], t3[3], xf.z, xf.w);
+            }
+            const float sig = ldsf(rec + kScaleOff + 4 * c);
+            const float s0 = __fmul_rn(half_bits_to_float(static_cast<uint16_t>(dh[0])), sig);
+            const float s1 = __fmul_rn(half_bits_to_float(static_cast<uint16_t>(dh[1])), sig);
+            const float s2 = __fmul_rn(half_bits_to_float(static_cast<uint16_t>(dh[2])), sig);
+            const float s3 = __fmul_rn(half_bits_to_float(static_cast<uint16_t>(dh[3])), sig);
+            acc[0] = fmaf(s0, d0[0] + d0[1], acc[0]);
+            acc[1] = fmaf(s1, d0[2] + d0[3], acc[1]);
+            acc[2] = fmaf(s2, d1[0] + d1[1], acc[2]);
+            acc[3] = fmaf(s3, d1[2] + d1[3], acc[3]);
+        }
+        // the last warp to finish a pair of this box releases the stage
+        __syncwarp();
+        if (lane == 0) {
+            if (atomicAdd(&done[s], 1) == width - 1) {
+                done[s] = 0;
+                mbar_arrive(&empty[s]);
+            }
+        }
+    }
+    if (cur >= 0) flush(cur);
+    for (; next_arrival <= t_last; ++next_arrival) arrive(next_arrival - t_first);
+}
+
+struct Q4MmaPlan {
+    int grid, tiles, ppr, max_tiles, stages, max_pairs;
+    long long units;
+    size_t smem;
+};
+
+bool q4_mma_plan(Q4MmaPlan &p, int k, int n, const DeviceInfo &dev) {
+    if (k % 256 != 0 || n <= 0) return false;
+    p.tiles = (n + kTileRows - 1) / kTileRows;
+    p.ppr = k / 256;
+    p.units = static_cast<long long>(p.tiles) * p.ppr;
+    p.grid = static_cast<int>(p.units < dev.sm_count ? p.units : dev.sm_count);
+    const long long per = (p.units + p.grid - 1) / p.grid;
+    p.max_tiles = static_cast<int>((per + p.ppr - 1) / p.ppr + 1);
+    p.max_pairs = static_cast<int>(per);
+    if (p.max_pairs > 8191) return false;  // pair index field of the box table
+    const size_t rest = static_cast<size_t>(k / 128) * kRecBytes + sizeof(float) * p.max_tiles * kWarps * 32 +
+                        16 * kMaxStages + 16 + 8 * kMaxStages + 4 * p.max_tiles + 4 * p.max_pairs + 2 * p.max_pairs + 16;
+    const size_t budget = static_cast<size_t>(dev.smem_optin) - 1024;
+    if (rest + 3 * static_cast<size_t>(kStageBytes) > budget) return false;
+    p.stages = static_cast<int>((budget - rest) / kStageBytes);
+    if (p.stages > kMaxStages) p.stages = kMaxStages;
+    p.smem = static_cast<size_t>(p.stages) * kStageBytes + rest;
+    return true;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        else
+            cudaGetLastError();
+    }
+    return fn;
+}
+
+// Tensor maps of a weight matrix, cached by (pointer, k, n).  Called with the
+// library's runtime mutex held.
+bool weight_maps(Q4MmaMaps &out, const void *w, int k, int n) {
+    struct Entry {
+        const void *w = nullptr;
+        int k = 0, n = 0;
+        Q4MmaMaps maps;
+    };
+    static Entry cache[16];
+    static int next = 0;
+    for (const Entry &e : cache)
+        if (e.w == w && e.k == k && e.n == n) {
+            out = e.maps;
+            return true;
+        }
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t row_bytes = static_cast<cuuint64_t>(k / 32) * 18;
+    cuuint64_t dims[2] = {row_bytes / 4, static_cast<cuuint64_t>(n)};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t estr[2] = {1, 1};
+    Q4MmaMaps maps;
+    for (int width = 1; width <= kMaxBoxPairs; width += 2) {
+        cuuint32_t box[2] = {static_cast<cuuint32_t>(kPairWords * width), kTileRows};
+        if (fn(&maps.box[map_of_width(width)], CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void *>(w), dims,
+               strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return false;
+    }
+    cache[next].w = w;
+    cache[next].k = k;
+    cache[next].n = n;
+    cache[next].maps = maps;
+    next = (next + 1) % 16;
+    out = maps;
+    return true;
+}
+
+}  // namespace
+
+size_t q4_mma_scratch_bytes(int k, int n, int batch, const DeviceInfo &dev) {
+    Q4MmaPlan p;
+    if (batch != 1 || !q4_mma_plan(p, k, n, dev)) return 0;
+    return static_cast<size_t>(p.grid) * 32 * sizeof(unsigned long long);
+}
+
+cudaError_t launch_q4_mma_gemv(const GemvRequest &r, const DeviceInfo &dev, cudaStream_t stream) {
+    Q4MmaPlan p;
+    if (r.wt != 2 || r.batch != 1 || !r.fixup || !q4_mma_plan(p, r.k, r.n, dev)) return cudaErrorNotSupported;
+    if ((reinterpret_cast<uintptr_t>(r.w) & 15) || (reinterpret_cast<uintptr_t>(r.x) & 15))
+        return cudaErrorNotSupported;
+    if (r.fixup_bytes < q4_mma_scratch_bytes(r.k, r.n, 1, dev)) return cudaErrorNotSupported;
+    Q4MmaMaps maps;
+    if (!weight_maps(maps, r.w, r.k, r.n)) return cudaErrorNotSupported;
+    Q4MmaArgs a{};
+    a.x = r.x;
+    a.y = r.y;
+    a.slot = static_cast<unsigned long long *>(r.fixup);
+    a.err = dev.err;
+    a.units = p.units;
+    a.k = r.k;
+    a.n = r.n;
+    a.tiles = p.tiles;
+    a.ppr = p.ppr;
+    a.grid = p.grid;
+    a.prefetch = r.prefetch_weights ? 1 << 30 : 0;
+    a.max_tiles = p.max_tiles;
+    a.stages = p.stages;
+    a.max_pairs = p.max_pairs;
+    static int configured[64] = {0};
+    int devno = 0;
+    cudaGetDevice(&devno);
+    if (devno < 0 || devno >= 64 || configured[devno] < static_cast<int>(p.smem)) {
+        cudaError_t e = cudaFuncSetAttribute(q4_mma_gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(p.smem));
+        if (e != cudaSuccess) return e;
+        if (devno >= 0 && devno < 64) configured[devno] = static_cast<int>(p.smem);
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(p.grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = p.smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, q4_mma_gemv_kernel, maps, a);
+}
+
+}  // namespace k200

@@ -28,10 +28,20 @@ struct GemvRequest {
     long long q_comp;              // elements between component 0 and 1 of q (wt 3)
     bool prefetch_weights;         // weights are not written by the preceding kernel: stream
                                    // them before that kernel completes (programmatic launch)
+    void *fixup = nullptr;         // Kernel-owned scratch of the tensor-core Q4_0 GEMV (counters
+    size_t fixup_bytes = 0;        // zeroed at allocation, partial sums), see q4_mma_scratch_bytes
 };
 
 // Streaming GEMV launcher (handles any batch by column groups).
 cudaError_t launch_gemv(const GemvRequest &r, const DeviceInfo &dev, cudaStream_t stream);
+
+// Tensor-core Q4_0 GEMV for one activation column (gemv_q4_mma.cu).  Scratch
+// it needs for this shape (0: shape not handled; the caller then leaves
+// GemvRequest::fixup empty and launch_gemv takes the streaming kernel): the
+// partial sums of row tiles shared between CTAs, which must be zero before
+// the first launch; every launch leaves them zero.
+size_t q4_mma_scratch_bytes(int k, int n, int batch, const DeviceInfo &dev);
+cudaError_t launch_q4_mma_gemv(const GemvRequest &r, const DeviceInfo &dev, cudaStream_t stream);
 bool gemv_fast_path_ok(int wt, const void *w, const void *x, const void *y, int k, long long row_bytes);
 
 // Per-tensor two-component A8 quantiser of the rowwise-int8 path

@@ -46,6 +46,7 @@ struct DeviceState {
     std::atomic<size_t> allocated{0};
     std::atomic<size_t> matmuls{0};
     bool static_weights = false;     // see k200_set_static_weights
+    bool q4_mma = true;              // tensor-core Q4_0 GEMV (KUNLUN_Q4_MMA=0 selects the FP32 kernel)
     void *noalloc_scratch = nullptr; // static scratch address (k200_matmul_i8_noalloc)
 };
 DeviceState devices[kMaxDevices];
@@ -100,6 +101,8 @@ DeviceState &state(int id) {
         d.info.err = dev_err;
         const char *sw = std::getenv("KUNLUN_STATIC_WEIGHTS");
         d.static_weights = sw && std::strcmp(sw, "1") == 0;
+        const char *qm = std::getenv("KUNLUN_Q4_MMA");
+        d.q4_mma = !(qm && std::strcmp(qm, "0") == 0);
         fail_cuda(cudaDeviceGetAttribute(&d.info.sm_count, cudaDevAttrMultiProcessorCount, id), "sm count");
         fail_cuda(cudaDeviceGetAttribute(&d.info.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, id),
                   "smem opt-in");
@@ -252,6 +255,8 @@ struct Kernel::Impl {
     void *params = nullptr;  // {max0, max1} + reduction words (256 bytes)
     void *alias = nullptr;   // elementwise broadcast operand copy when y aliases b
     size_t alias_size = 0;
+    void *fixup = nullptr;   // tensor-core Q4_0 GEMV: tile counters (zeroed) + partial sums
+    size_t fixup_size = 0;
 };
 
 Kernel::Kernel() : impl_(new Impl{}) {}
@@ -264,6 +269,7 @@ Kernel::~Kernel() {
         release(s.id, s.quant, s.quant_size);
         release(s.id, s.params, 256);
         release(s.id, s.alias, s.alias_size);
+        release(s.id, s.fixup, s.fixup_size);
     }
     delete impl_;
 }
@@ -332,6 +338,16 @@ void matmul(Kernel &kernel, int id, void *y, const void *w, const void *x, int k
         r.row_scale = scales;
     } else {
         r.x = static_cast<const float *>(x);
+        const size_t need = type == WeightType::q4_0 && d.q4_mma ? k200::q4_mma_scratch_bytes(k, n, batch, d.info) : 0;
+        if (need) {
+            if (s.fixup_size < need) {
+                grow(s, s.fixup, s.fixup_size, need);
+                // arrival counters start at zero; every launch leaves them zero
+                fail_cuda(cudaMemsetAsync(s.fixup, 0, need, d.stream), "cudaMemsetAsync(fixup)");
+            }
+            r.fixup = s.fixup;
+            r.fixup_bytes = s.fixup_size;
+        }
     }
     check((int)k200::launch_gemv(r, d.info, d.stream));
     ++d.matmuls;

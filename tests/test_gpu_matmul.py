@@ -82,6 +82,11 @@ def _q4_case(O, k, n, batch, seed=0x7340D123):
         (32, 1, 1),          # smallest legal shape
         (8224, 17, 2),       # K % 256 != 0: rows not 16-byte multiples
         (4096, 300, 9),      # several column groups
+        (256, 33, 1),        # tensor-core path: one box per row, N tail
+        (1024, 5000, 1),     # tensor-core path: several row tiles per CTA
+        (16384, 32, 1),      # one row tile split over many CTAs (cross-CTA sums)
+        (16384, 100, 1),     # largest K, partial last tile
+        (4352, 2049, 1),     # K/256 odd, N = 64*32 + 1
     ],
 )
 def test_q4_0_matches_fp64_gold(K, O, gpu, k, n, batch):
@@ -103,17 +108,32 @@ def test_q4_0_library_bench_closed_form(K, O, gpu):
     assert (np.abs(y - gold) <= 1e-3 * (1 + np.abs(gold))).all()
 
 
-def test_q4_0_reference_fixture(K, O, gpu):
+@pytest.mark.parametrize("batch", [1, 2])
+def test_q4_0_reference_fixture(K, O, gpu, batch):
     """native_q4_bench fixtures (random scales incl. zero scales, patterns 0/1/4)."""
     k, n = 512, 64
     q4 = O.fixture_q4(k, n)
     for pattern in (0, 1, 4):
-        x = O.fixture_input(k, 2, pattern)
-        y = _device_matmul(K, K.Q4_0, q4, x, k, n, 2)
-        gold = O.matmul_gold(q4, O.WT_Q4_0, x, k, n, 2)
-        _check_float(y, gold, _abs_gold(O, q4, O.WT_Q4_0, x, k, n, 2))
+        x = O.fixture_input(k, batch, pattern)
+        y = _device_matmul(K, K.Q4_0, q4, x, k, n, batch)
+        gold = O.matmul_gold(q4, O.WT_Q4_0, x, k, n, batch)
+        _check_float(y, gold, _abs_gold(O, q4, O.WT_Q4_0, x, k, n, batch))
         # the reference's exact-path bar (native_q4_bench: NMSE < 1e-10)
         assert np.sum((y - gold) ** 2) / np.sum(gold ** 2) < 1e-10
+
+
+def test_q4_0_activation_range(K, O, gpu):
+    """Activation blocks from 1e-30 to 1e30 (and an all-zero block) keep FP32 accuracy."""
+    k, n = 2048, 96
+    q4, x = _q4_case(O, k, n, 1)
+    scale = np.repeat(np.float32(10.0) ** np.linspace(-30, 30, k // 32).astype(np.float32), 32)
+    x = (x * scale).astype(np.float32)
+    x[64:96] = 0.0
+    y = _device_matmul(K, K.Q4_0, q4, x, k, n, 1)
+    gold = O.matmul_gold(q4, O.WT_Q4_0, x, k, n, 1)
+    absgold = _abs_gold(O, q4, O.WT_Q4_0, x, k, n, 1)
+    # relative to the conditioning of each dot product (outputs reach 1e29)
+    assert (np.abs(y - gold) <= 64 * 2.0 ** -24 * absgold).all()
 
 
 def test_q4_0_unaligned_pointers(K, O, gpu):
