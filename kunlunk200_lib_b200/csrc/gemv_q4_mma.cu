@@ -69,7 +69,7 @@ constexpr int kPairWords = kPairBytes / 4;
 constexpr int kGroupBytes = 72;
 constexpr int kMaxBoxPairs = 7;                        // widest box: 32 rows x 1008 bytes
 constexpr int kStageBytes = kTileRows * kPairBytes * kMaxBoxPairs;  // 32256
-constexpr int kMaxStages = 8;
+constexpr int kStages = 4;                             // ring stages: 4 x 32 KB in flight streams at ~6 TB/s
 constexpr int kRecBytes = 544;                         // fragment record of one group
 constexpr int kZeroOff = 512, kScaleOff = 528;
 constexpr int kWarps = 16;                             // consumer warps
@@ -83,8 +83,6 @@ struct Q4MmaArgs {
     long long units;    // row tiles * pairs per row
     int k, n, tiles, ppr, grid, prefetch;
     int max_tiles;      // row tiles any CTA touches (partial-sum slots in shared memory)
-    int stages;         // ring stages (<= kMaxStages)
-    int max_pairs;      // pairs any CTA processes (box tables in shared memory)
 };
 
 // Tensor maps over the weight rows viewed as 32-bit words [n][row_bytes/4],
@@ -94,9 +92,10 @@ struct Q4MmaMaps {
 };
 __host__ __device__ constexpr int map_of_width(int w) { return (kMaxBoxPairs - w) / 2; }
 
-// The CTA's pairs [u, end) covered by boxes: as wide as possible (7 pairs),
-// never across a row tile, odd widths only.  Producer and consumers walk the
-// same sequence.
+// The CTA's pairs [u, end) covered by boxes: each row tile's part of the
+// range is cut into 7-pair boxes and a remainder r < 7 (r odd: one r-pair
+// box; r even: an (r-1)-pair and a 1-pair box).  The producer walks this
+// sequence; consumers locate a pair in it with box_of().
 struct BoxWalk {
     long long u, end;
     int tile, pair, width, ppr;
@@ -116,6 +115,34 @@ struct BoxWalk {
         fit();
     }
 };
+
+// Boxes that cover a segment of L pairs.
+__device__ __forceinline__ int boxes_in(int L) {
+    const int f = L / 7, r = L - 7 * f;
+    return f + (r == 0 ? 0 : (r & 1) ? 1 : 2);
+}
+
+// Position of a pair in the box sequence: segment [s0, s1) of its row tile
+// (pairs in row), its pair index p in the row, the boxes before the segment.
+struct BoxPos {
+    int box, q, width;  // box index in the CTA's sequence, pair within box, box width
+};
+__device__ __forceinline__ BoxPos box_of(int p, int s0, int s1, int before) {
+    const int o = p - s0, L = s1 - s0;
+    const int f = L / 7, r = L - 7 * f;
+    BoxPos b;
+    if (o < 7 * f) {
+        b.box = o / 7;
+        b.q = o - 7 * b.box;
+        b.width = 7;
+    } else {
+        const int o2 = o - 7 * f, w1 = (r & 1) ? r : r - 1;
+        if (o2 < w1) { b.box = f; b.q = o2; b.width = w1; }
+        else { b.box = f + 1; b.q = 0; b.width = 1; }
+    }
+    b.box += before;
+    return b;
+}
 
 // Column pair c of the MMA carries block beta(c) of a group, beta = (3, 1, 2, 0),
 // and lane c of a quad finishes that block; beta_inv is the inverse.
@@ -310,18 +337,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     q4_mma_gemv_kernel(const __grid_constant__ Q4MmaMaps maps, const Q4MmaArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int groups = a.k >> 7;
-    const int S = a.stages;
+    constexpr int S = kStages;
     uint8_t *ring = smem;
     uint8_t *xrec = ring + S * kStageBytes;
     float *part = reinterpret_cast<float *>(xrec + groups * kRecBytes);  // [max_tiles][kWarps][32]
     uint64_t *full = reinterpret_cast<uint64_t *>(part + a.max_tiles * kWarps * 32);
-    uint64_t *empty = full + kMaxStages;
-    uint64_t *tables = empty + kMaxStages;                                       // box tables written
-    volatile int *seqno = reinterpret_cast<volatile int *>(tables + 2);         // box held by each stage
-    int *done = const_cast<int *>(seqno) + kMaxStages;                          // pairs finished per stage
-    int *tcnt = done + kMaxStages;                                               // [max_tiles] warp arrivals
-    uint32_t *boxinfo = reinterpret_cast<uint32_t *>(tcnt + a.max_tiles);      // [boxes] see below
-    uint16_t *pairbox = reinterpret_cast<uint16_t *>(boxinfo + a.max_pairs);   // [pairs] box << 3 | pair in box
+    uint64_t *empty = full + S;
+    volatile int *seqno = reinterpret_cast<volatile int *>(empty + S);  // box held by each stage
+    int *done = const_cast<int *>(seqno) + S;                          // pairs finished per stage
+    int *tcnt = done + S;                                               // [max_tiles] warp arrivals
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const long long u0 = static_cast<long long>(blockIdx.x) * a.units / a.grid;
@@ -333,7 +357,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (tid < S) {
         mbar_init(&full[tid], 1);
         mbar_init(&empty[tid], 1);
-        if (tid == 0) mbar_init(tables, 1);
         fence_mbar_init();
         seqno[tid] = -1;
         done[tid] = 0;
@@ -365,17 +388,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             // never exit with a copy still writing into this CTA's shared memory
             for (int i = j > S ? j - S : 0; i < j; ++i)
                 (void)mbar_wait(&full[i % S], (i / S) & 1, a.err, kErrBulkTimeout);
-        } else if (lane == 1) {
-            // the same box sequence, tabulated for the consumers: boxinfo[j] =
-            // tile offset (bits 16..), pair in row (8..15), width (4..7),
-            // stage (1..3), mbarrier parity (0); pairbox[i] = box << 3 | pair in box
-            int j = 0, st = 0, ph = 0;
-            for (BoxWalk bw(u0, u1, a.ppr); bw.u < u1; bw.next(), ++j) {
-                boxinfo[j] = static_cast<uint32_t>((bw.tile - t_first) << 16 | bw.pair << 8 | bw.width << 4 | st << 1 | ph);
-                for (int q = 0; q < bw.width; ++q) pairbox[bw.u - u0 + q] = static_cast<uint16_t>(j << 3 | q);
-                if (++st == S) { st = 0; ph ^= 1; }
-            }
-            mbar_arrive(tables);  // release: the tables are visible to waiters of this phase
         }
         return;
     }
@@ -403,7 +415,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = tid; i < a.max_tiles * kWarps * 32; i += kWarps * 32) part[i] = 0.f;
     consumer_sync();
-    if (!mbar_wait(tables, 0, a.err, kErrBulkTimeout)) return;
 
     const int g = lane >> 2, c = lane & 3;
     // The five words lane c loads from each of its rows, as byte offsets in
@@ -499,12 +510,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         next_arrival = t + 1;
     };
 
+    // this CTA's range in pair coordinates: first/last row tile, where the
+    // range starts in the first one and ends in the last one, and the boxes
+    // of the first segment and of a full row
+    const int p_first = static_cast<int>(u0 - static_cast<long long>(t_first) * a.ppr);
+    const int p_end = static_cast<int>(u1 - static_cast<long long>(t_last) * a.ppr);
+    const int boxes_first = boxes_in((t_first == t_last ? p_end : a.ppr) - p_first);
+    const int boxes_row = boxes_in(a.ppr);
+    int tile = t_first, p = p_first + warp;
+    while (p >= a.ppr) { p -= a.ppr; ++tile; }
     for (int i = warp; i < nu; i += kWarps) {
-        const uint32_t pb = pairbox[i];
-        const int j = static_cast<int>(pb >> 3), q = static_cast<int>(pb & 7);
-        const uint32_t info = boxinfo[j];
-        const int s = (info >> 1) & 7, width = (info >> 4) & 15;
-        const int tile = t_first + static_cast<int>(info >> 16);
+        const int s0 = tile == t_first ? p_first : 0, s1 = tile == t_last ? p_end : a.ppr;
+        const int before = tile == t_first ? 0 : boxes_first + (tile - t_first - 1) * boxes_row;
+        const BoxPos bp = box_of(p, s0, s1, before);
+        const int j = bp.box, q = bp.q, width = bp.width;
+        const int s = j & (S - 1);
         // wait until the stage holds box j, then for its bytes
         if (seqno[s] != j) {
             bool ok = true;
@@ -514,7 +534,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (!ok) break;
         }
-        if (!mbar_wait(&full[s], info & 1, a.err, kErrBulkTimeout)) break;
+        if (!mbar_wait(&full[s], (j / S) & 1, a.err, kErrBulkTimeout)) break;
         if (tile != cur) {
             if (cur >= 0) flush(cur);
             for (; next_arrival < tile; ++next_arrival) arrive(next_arrival - t_first);
@@ -524,7 +544,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // this lane's rows g, g+8, g+16, g+24 of the pair, at byte 4c of each group
         const uint32_t r0 = ring_u + s * kStageBytes + q * kPairBytes + g * pitch + 4 * c;
         const uint32_t rows[4] = {r0, r0 + 8 * pitch, r0 + 16 * pitch, r0 + 24 * pitch};
-        const uint32_t recp = xrec_u + (((info >> 8) & 255) + q) * 2 * kRecBytes;
+        const uint32_t recp = xrec_u + p * 2 * kRecBytes;
 #pragma unroll
         for (int grp = 0; grp < 2; ++grp) {
             const uint32_t rec = recp + grp * kRecBytes;
@@ -575,13 +595,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_arrive(&empty[s]);
             }
         }
+        p += kWarps;
+        while (p >= a.ppr) { p -= a.ppr; ++tile; }
     }
     if (cur >= 0) flush(cur);
     for (; next_arrival <= t_last; ++next_arrival) arrive(next_arrival - t_first);
 }
 
 struct Q4MmaPlan {
-    int grid, tiles, ppr, max_tiles, stages, max_pairs;
+    int grid, tiles, ppr, max_tiles;
     long long units;
     size_t smem;
 };
@@ -594,16 +616,9 @@ bool q4_mma_plan(Q4MmaPlan &p, int k, int n, const DeviceInfo &dev) {
     p.grid = static_cast<int>(p.units < dev.sm_count ? p.units : dev.sm_count);
     const long long per = (p.units + p.grid - 1) / p.grid;
     p.max_tiles = static_cast<int>((per + p.ppr - 1) / p.ppr + 1);
-    p.max_pairs = static_cast<int>(per);
-    if (p.max_pairs > 8191) return false;  // pair index field of the box table
-    const size_t rest = static_cast<size_t>(k / 128) * kRecBytes + sizeof(float) * p.max_tiles * kWarps * 32 +
-                        16 * kMaxStages + 16 + 8 * kMaxStages + 4 * p.max_tiles + 4 * p.max_pairs + 2 * p.max_pairs + 16;
-    const size_t budget = static_cast<size_t>(dev.smem_optin) - 1024;
-    if (rest + 3 * static_cast<size_t>(kStageBytes) > budget) return false;
-    p.stages = static_cast<int>((budget - rest) / kStageBytes);
-    if (p.stages > kMaxStages) p.stages = kMaxStages;
-    p.smem = static_cast<size_t>(p.stages) * kStageBytes + rest;
-    return true;
+    p.smem = static_cast<size_t>(kStages) * kStageBytes + static_cast<size_t>(k / 128) * kRecBytes +
+             sizeof(float) * p.max_tiles * kWarps * 32 + 16 * kStages + 8 * kStages + 4 * p.max_tiles + 16;
+    return p.smem + 1024 <= static_cast<size_t>(dev.smem_optin);
 }
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
@@ -690,8 +705,6 @@ cudaError_t launch_q4_mma_gemv(const GemvRequest &r, const DeviceInfo &dev, cuda
     a.grid = p.grid;
     a.prefetch = r.prefetch_weights ? 1 << 30 : 0;
     a.max_tiles = p.max_tiles;
-    a.stages = p.stages;
-    a.max_pairs = p.max_pairs;
     static int configured[64] = {0};
     int devno = 0;
     cudaGetDevice(&devno);
