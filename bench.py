@@ -258,10 +258,12 @@ def run_ours(args) -> None:
     K.set_stream(dev, stream.cuda_stream)
     l2 = torch.cuda.get_device_properties(dev).L2_cache_size
 
+    from kunlunk200_lib_b200.shard import row_shard
+
     for k, n in (UP, DOWN):
-        if n % world:
-            raise SystemExit(f"N={n} does not split over {world} GPUs")
-    n_up, n_down = UP[1] // world, DOWN[1] // world
+        if n % world:  # equal slices: the all-gather writes Y without padding
+            raise SystemExit(f"N={n} does not split evenly over {world} GPUs")
+    n_up, n_down = row_shard(UP[1], world, rank)[1], row_shard(DOWN[1], world, rank)[1]
     shard_bytes = q4_bytes(UP[0], n_up) + q4_bytes(DOWN[0], n_down)
     total_bytes = q4_bytes(*UP) + q4_bytes(*DOWN)
     sets = max(2, math.ceil(2 * l2 / shard_bytes) + 1)

@@ -1,0 +1,86 @@
+"""Row sharding + all-gather of the multi-GPU matmul path, on CPU.
+
+The arithmetic of every output row is independent of the sharding, so the
+gathered result must equal the unsharded oracle result bit for bit.  Two
+`gloo` ranks stand in for two GPUs (the data path on GPUs is the same
+host logic with NCCL)."""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from kunlunk200_lib_b200.shard import gather_rows, padded_rows, row_shard
+
+
+@pytest.mark.parametrize("n,world", [(11008, 8), (4096, 2), (8193, 4), (5, 8), (1, 2), (14336, 3)])
+def test_row_shard_covers_rows_once(n, world):
+    seen = []
+    for r in range(world):
+        start, count = row_shard(n, world, r)
+        assert count <= padded_rows(n, world)
+        seen.extend(range(start, start + count))
+    assert seen == list(range(n))
+
+
+def test_gather_rows_numpy_roundtrip():
+    n, world, batch = 10, 4, 3
+    full = np.arange(batch * n, dtype=np.float32).reshape(batch, n)
+    pad = padded_rows(n, world)
+    blocks = np.zeros((world, batch, pad), np.float32)
+    for r in range(world):
+        s, c = row_shard(n, world, r)
+        blocks[r, :, :c] = full[:, s:s + c]
+    assert np.array_equal(gather_rows(blocks.ravel(), n, world, batch), full)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank, world, port, k, n, batch, q4, x, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import oracle as O
+
+        start, count = row_shard(n, world, rank)
+        row_bytes = k // 32 * 18
+        shard = q4[start * row_bytes:(start + count) * row_bytes]
+        y = O.matmul_gold(shard, O.WT_Q4_0, x, k, count, batch).astype(np.float32).reshape(batch, count)
+        pad = padded_rows(n, world)
+        mine = torch.zeros(batch, pad)
+        mine[:, :count] = torch.from_numpy(y)
+        gathered = torch.empty(world * batch * pad)
+        dist.all_gather_into_tensor(gathered, mine.reshape(-1))
+        if rank == 0:
+            out.put(gather_rows(gathered, n, world, batch).numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("n,batch", [(4096, 1), (1001, 2)])
+def test_sharded_q4_gemv_matches_unsharded(O, n, batch):
+    k, world = 256, 2
+    w = O.normal(0x7340D123, n * k, 0.0, 0.02)
+    q4 = O.q4_0_quantize(w, n, k)
+    x = O.uniform(0x09200ABC, k * batch, -1.0, 1.0)
+    full = O.matmul_gold(q4, O.WT_Q4_0, x, k, n, batch).astype(np.float32).reshape(batch, n)
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, world, port, k, n, batch, q4, x, out)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = out.get(timeout=120)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert np.array_equal(got, full)
