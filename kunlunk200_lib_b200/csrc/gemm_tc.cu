@@ -1,0 +1,319 @@
+// Batched matmul on the 5th-generation tensor cores (tcgen05, sm_100a):
+// Y[b, n] = X[b, :] . W[n, :] for batches of activation columns, the
+// "matmul" of src/k200.cpp:268-279 when batch is large enough that the
+// weight rows are reused across columns (the streaming GEMV kernels re-read W
+// once per pair of columns).
+//
+// One CTA computes a tile of 128 weight rows x NB activation columns:
+//  * warp 0 (one thread) streams the K dimension through a ring of stages
+//    with 2-D TMA copies in the 128-byte-swizzled K-major layout the MMA reads
+//    directly: the weight tile (128 rows x 128 bytes) and up to two
+//    activation operands (NB rows x 128 bytes);
+//  * warp 1 allocates tensor memory, and one of its threads issues the
+//    tcgen05.mma instructions (M = 128, N = NB) for every 128-byte K step and
+//    releases each stage with tcgen05.commit when its MMAs are done;
+//  * warps 2-5 wait for the last commit, read the accumulators from tensor
+//    memory (tcgen05.ld, 32 lanes = 32 weight rows per warp) and write Y,
+//    consecutive lanes writing consecutive outputs of a column.
+//
+// Operand sets (Mode):
+//  * kI8: rowwise-int8 weights x the two int8 activation components of the
+//    per-tensor two-pass quantiser (src/k200.cpp:209-239), kind::i8 with two
+//    int32 accumulators; the epilogue is the combine of
+//    kernels/kunlun-combine.xpu:19, so results are bit-exact with the
+//    reference's integer dot products.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstdint>
+#include <cstdio>
+
+#include "device_common.cuh"
+#include "k200_internal.h"
+
+namespace k200 {
+
+namespace {
+
+constexpr int kTileM = 128;       // weight rows per CTA (MMA M)
+constexpr int kStepBytes = 128;   // K bytes per pipeline step (one 128-byte swizzle atom)
+constexpr int kThreadsTc = 192;   // 6 warps: TMA, MMA, 4 x epilogue
+
+enum Mode : int { kI8 = 0 };
+
+struct TcMaps {
+    CUtensorMap a;    // weights [n][k] (bytes)
+    CUtensorMap b0;   // activation operand 0 [batch][k]
+    CUtensorMap b1;   // activation operand 1 [batch][k]
+};
+
+struct TcArgs {
+    float *y;
+    const float *row_scale;  // rowwise-int8: per weight row scale
+    const float *act_max;    // rowwise-int8: {max0, max1}
+    int *err;
+    int k, n, batch, y_stride;
+    int nb;                  // activation columns per CTA (MMA N, multiple of 16)
+    int stages;
+    int ksteps;
+    uint32_t tmem_cols;      // allocated tensor-memory columns (power of two >= 32)
+};
+
+// ---- tcgen05 primitives ----------------------------------------------------
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t cols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major operand tile stored in the
+// 128-byte swizzled layout TMA writes (8-row groups of 1024 bytes): start
+// address, leading offset 16 B (unused for swizzled K-major), stride 1024 B
+// between 8-row groups, descriptor version 1, layout SWIZZLE_128B.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((saddr >> 4) & 0x3fff);
+    d |= static_cast<uint64_t>(1) << 16;                 // LBO = 16 B
+    d |= static_cast<uint64_t>(1024 >> 4) << 32;         // SBO = 1024 B
+    d |= static_cast<uint64_t>(1) << 46;                 // version
+    d |= static_cast<uint64_t>(2) << 61;                 // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor: D format (0 f16, 1 f32, 2 s32), A/B formats, both
+// K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+__host__ __device__ constexpr uint32_t instr_desc(uint32_t dfmt, uint32_t afmt, uint32_t bfmt, int m, int n) {
+    return (dfmt << 4) | (afmt << 7) | (bfmt << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+           (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// ---- the kernel --------------------------------------------------------------
+template <int MODE>
+__global__ void __launch_bounds__(kThreadsTc, 1) gemm_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // 1024-byte aligned stages: [A 128 x 128 B][B0 nb x 128 B][B1 nb x 128 B]
+    const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+    uint8_t *smem = smem_raw + (base - smem_u32(smem_raw));
+    const uint32_t a_bytes = kTileM * kStepBytes, b_bytes = a.nb * kStepBytes;
+    const uint32_t stage_bytes = a_bytes + 2 * b_bytes;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + a.stages * stage_bytes);
+    uint64_t *empty = full + a.stages;
+    uint64_t *accum = empty + a.stages;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * kTileM, n0 = blockIdx.y * a.nb;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < a.stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accum, 1);
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, a.tmem_cols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t taddr = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            pdl_wait_prior();
+            for (int ks = 0; ks < a.ksteps; ++ks) {
+                const int s = ks % a.stages;
+                if (ks >= a.stages && !mbar_wait(&empty[s], ((ks / a.stages) - 1) & 1, a.err, kErrBulkTimeout)) break;
+                const uint32_t st = base + s * stage_bytes;
+                mbar_arrive_expect_tx(&full[s], stage_bytes);
+                tma_2d(st, &maps.a, ks * kStepBytes, m0, &full[s]);
+                tma_2d(st + a_bytes, &maps.b0, ks * kStepBytes, n0, &full[s]);
+                tma_2d(st + a_bytes + b_bytes, &maps.b1, ks * kStepBytes, n0, &full[s]);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            const uint32_t idesc = instr_desc(2, 1, 1, kTileM, a.nb);  // s32 <- s8 x s8
+            for (int ks = 0; ks < a.ksteps; ++ks) {
+                const int s = ks % a.stages;
+                if (!mbar_wait(&full[s], (ks / a.stages) & 1, a.err, kErrBulkTimeout)) break;
+                tc_fence_after();
+                const uint32_t st = base + s * stage_bytes;
+                const uint64_t da = sw128_desc(st), db0 = sw128_desc(st + a_bytes), db1 = sw128_desc(st + a_bytes + b_bytes);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {  // 4 x K32 per 128-byte step; +32 bytes = +2 in the address field
+                    const uint32_t acc = (ks | kk) != 0;
+                    mma_i8(taddr, da + 2 * kk, db0 + 2 * kk, idesc, acc);
+                    mma_i8(taddr + a.nb, da + 2 * kk, db1 + 2 * kk, idesc, acc);
+                }
+                mma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+            }
+            mma_commit(accum);
+        }
+        __syncwarp();
+    } else {
+        // ---------------- epilogue: warps 2..5 -> TMEM lane quarters 2,3,0,1 ----------------
+        const int quarter = warp & 3;
+        const int row = m0 + quarter * 32 + lane;  // weight row of this thread
+        const bool ok = mbar_wait(accum, 0, a.err, kErrMmaTimeout);
+        tc_fence_after();
+        if (ok) {
+            const float s0 = __fdiv_rn(a.act_max[0], 127.0f), s1 = __fdiv_rn(a.act_max[1], 127.0f);
+            const float rs = row < a.n ? a.row_scale[row] : 0.f;
+            const uint32_t lane_addr = taddr + (static_cast<uint32_t>(quarter * 32) << 16);
+            for (int c0 = 0; c0 < a.nb; c0 += 16) {
+                uint32_t p0[16], p1[16];
+                tmem_ld16(lane_addr + c0, p0);
+                tmem_ld16(lane_addr + a.nb + c0, p1);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int col = n0 + c0 + i;
+                    if (row < a.n && col < a.batch) {
+                        const float t0 = __fmul_rn(static_cast<float>(static_cast<int>(p0[i])), s0);
+                        const float t1 = __fmul_rn(static_cast<float>(static_cast<int>(p1[i])), s1);
+                        a.y[static_cast<long long>(col) * a.y_stride + row] = __fmul_rn(__fadd_rn(t0, t1), rs);
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(taddr, a.tmem_cols);
+    }
+}
+
+// ---- host side -------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 tc_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        else
+            cudaGetLastError();
+    }
+    return fn;
+}
+
+// [rows][k] bytes, boxes of box_rows x 128 bytes, 128-byte swizzle.
+bool encode_kmajor(CUtensorMap &m, const void *ptr, long long row_bytes, int rows, int box_rows) {
+    auto fn = tc_encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(kStepBytes), static_cast<cuuint32_t>(box_rows)};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+bool gemm_tc_supported(int wt, int k, int n, int batch) {
+    (void)n;
+    return wt == 3 && batch >= kTcMinBatch && k % 16 == 0;
+}
+
+cudaError_t launch_gemm_tc(const GemvRequest &r, const DeviceInfo &dev, cudaStream_t stream) {
+    if (!gemm_tc_supported(r.wt, r.k, r.n, r.batch)) return cudaErrorNotSupported;
+    if ((reinterpret_cast<uintptr_t>(r.w) & 15) || (reinterpret_cast<uintptr_t>(r.q) & 15) || (r.q_comp & 15) ||
+        r.q_stride != r.k)
+        return cudaErrorNotSupported;
+    TcArgs a{};
+    a.y = r.y;
+    a.row_scale = r.row_scale;
+    a.act_max = r.act_max;
+    a.err = dev.err;
+    a.k = r.k;
+    a.n = r.n;
+    a.batch = r.batch;
+    a.y_stride = r.y_stride;
+    a.nb = r.batch >= 256 ? 256 : (r.batch + 15) / 16 * 16;
+    a.ksteps = (r.k + kStepBytes - 1) / kStepBytes;
+    uint32_t cols = 32;
+    while (cols < static_cast<uint32_t>(2 * a.nb)) cols <<= 1;
+    a.tmem_cols = cols;
+    const size_t stage = static_cast<size_t>(kTileM) * kStepBytes + 2 * static_cast<size_t>(a.nb) * kStepBytes;
+    const size_t budget = static_cast<size_t>(dev.smem_optin) - 1024 - 256;
+    int stages = static_cast<int>(budget / stage);
+    if (stages > 6) stages = 6;
+    if (stages < 2) return cudaErrorNotSupported;
+    a.stages = stages;
+    const size_t smem = 1024 + stages * stage + 256;
+    TcMaps maps;
+    if (!encode_kmajor(maps.a, r.w, r.k, r.n, kTileM) || !encode_kmajor(maps.b0, r.q, r.k, r.batch, a.nb) ||
+        !encode_kmajor(maps.b1, r.q + r.q_comp, r.k, r.batch, a.nb))
+        return cudaErrorNotSupported;
+    auto kern = gemm_tc_kernel<kI8>;
+    static int configured[64] = {0};
+    int devno = 0;
+    cudaGetDevice(&devno);
+    if (devno < 0 || devno >= 64 || configured[devno] < static_cast<int>(smem)) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+        if (devno >= 0 && devno < 64) configured[devno] = static_cast<int>(smem);
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((r.n + kTileM - 1) / kTileM, (r.batch + a.nb - 1) / a.nb);
+    cfg.blockDim = dim3(kThreadsTc);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, maps, a);
+}
+
+}  // namespace k200

@@ -761,6 +761,10 @@ cudaError_t launch_generic(const GemvRequest &r, int c0, int cols, long long row
 }  // namespace
 
 cudaError_t launch_gemv(const GemvRequest &r, const DeviceInfo &dev, cudaStream_t stream) {
+    if (r.tensor_cores && gemm_tc_supported(r.wt, r.k, r.n, r.batch)) {
+        const cudaError_t e = launch_gemm_tc(r, dev, stream);
+        if (e != cudaErrorNotSupported) return e;
+    }
     if (r.fixup) {
         const cudaError_t e = launch_q4_mma_gemv(r, dev, stream);
         if (e != cudaErrorNotSupported) return e;

@@ -47,6 +47,7 @@ struct DeviceState {
     std::atomic<size_t> matmuls{0};
     bool static_weights = false;     // see k200_set_static_weights
     bool q4_mma = true;              // tensor-core Q4_0 GEMV (KUNLUN_Q4_MMA=0 selects the FP32 kernel)
+    bool tensor_cores = true;        // tcgen05 GEMM for batched shapes (KUNLUN_TC=0: streaming kernels only)
     void *noalloc_scratch = nullptr; // static scratch address (k200_matmul_i8_noalloc)
 };
 DeviceState devices[kMaxDevices];
@@ -103,6 +104,8 @@ DeviceState &state(int id) {
         d.static_weights = sw && std::strcmp(sw, "1") == 0;
         const char *qm = std::getenv("KUNLUN_Q4_MMA");
         d.q4_mma = !(qm && std::strcmp(qm, "0") == 0);
+        const char *tc = std::getenv("KUNLUN_TC");
+        d.tensor_cores = !(tc && std::strcmp(tc, "0") == 0);
         fail_cuda(cudaDeviceGetAttribute(&d.info.sm_count, cudaDevAttrMultiProcessorCount, id), "sm count");
         fail_cuda(cudaDeviceGetAttribute(&d.info.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, id),
                   "smem opt-in");
@@ -320,6 +323,7 @@ void matmul(Kernel &kernel, int id, void *y, const void *w, const void *x, int k
     r.x_stride = k;
     r.y_stride = n;
     r.prefetch_weights = d.static_weights;
+    r.tensor_cores = d.tensor_cores;
     if (type == WeightType::rowwise_i8) {
         const size_t count = (size_t)k * batch;
         grow(s, s.quant, s.quant_size, aligned(2 * count));

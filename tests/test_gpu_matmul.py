@@ -216,7 +216,10 @@ def _i8_case(K, O, k, n, batch, seed=0x7340D123):
     return w, x, y, packed
 
 
-@pytest.mark.parametrize("k,n,batch", [(256, 65, 4), (8192, 1024, 1), (8192, 512, 32), (4096, 300, 9), (32, 3, 1)])
+@pytest.mark.parametrize("k,n,batch", [(256, 65, 4), (8192, 1024, 1), (8192, 512, 32), (4096, 300, 9), (32, 3, 1),
+                                       (8192, 2048, 256),   # config 4 shape class (tcgen05 kind::i8)
+                                       (1056, 1000, 300),   # two batch tiles, K not a multiple of 128
+                                       (96, 129, 17)])      # N and batch tails
 def test_rowwise_i8_bit_exact(K, O, gpu, k, n, batch):
     w, x, y, packed = _i8_case(K, O, k, n, batch)
     wq, scales = O.i8_pack_rows(w, k, n)
