@@ -16,12 +16,22 @@
 //    memory (tcgen05.ld, 32 lanes = 32 weight rows per warp) and write Y,
 //    consecutive lanes writing consecutive outputs of a column.
 //
-// Operand sets (Mode):
-//  * kI8: rowwise-int8 weights x the two int8 activation components of the
+// Operand sets:
+//  * rowwise-int8 (gemm_i8_kernel): weights x the two int8 activation components of the
 //    per-tensor two-pass quantiser (src/k200.cpp:209-239), kind::i8 with two
 //    int32 accumulators; the epilogue is the combine of
 //    kernels/kunlun-combine.xpu:19, so results are bit-exact with the
 //    reference's integer dot products.
+//  * f16 weights (gemm_f16_kernel): exact f16 weights x the activations split
+//    into f16 hi + lo parts after a power-of-two scaling per activation row
+//    (split_rows below; x = 2^e * (hi + lo) to about 22 bits), kind::f16.
+//    The tensor cores' f32 accumulation aligns each MMA to the running sum,
+//    which over K = 8192 costs ~2^-21 of sum|w*x| (measured); so the MMAs
+//    of every 4 K steps go to one of two tensor-memory slots and the
+//    epilogue warps add each finished slot into f32 registers while the
+//    other slot fills.  The reference computes these products in FP32
+//    (kernels/kunlun-matvec.xpu); the difference is the ~2^-22 split plus
+//    the order of the f32 sums.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -39,8 +49,6 @@ constexpr int kTileM = 128;       // weight rows per CTA (MMA M)
 constexpr int kStepBytes = 128;   // K bytes per pipeline step (one 128-byte swizzle atom)
 constexpr int kThreadsTc = 192;   // 6 warps: TMA, MMA, 4 x epilogue
 
-enum Mode : int { kI8 = 0 };
-
 struct TcMaps {
     CUtensorMap a;    // weights [n][k] (bytes)
     CUtensorMap b0;   // activation operand 0 [batch][k]
@@ -51,6 +59,7 @@ struct TcArgs {
     float *y;
     const float *row_scale;  // rowwise-int8: per weight row scale
     const float *act_max;    // rowwise-int8: {max0, max1}
+    const float *col_scale;  // f16: 2^e of each activation row
     int *err;
     int k, n, batch, y_stride;
     int nb;                  // activation columns per CTA (MMA N, multiple of 16)
@@ -103,6 +112,16 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t
         : "memory");
 }
 
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
@@ -126,8 +145,7 @@ __device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap *map, int
 }
 
 // ---- the kernel --------------------------------------------------------------
-template <int MODE>
-__global__ void __launch_bounds__(kThreadsTc, 1) gemm_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
+__global__ void __launch_bounds__(kThreadsTc, 1) gemm_i8_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte aligned stages: [A 128 x 128 B][B0 nb x 128 B][B1 nb x 128 B]
     const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
@@ -182,7 +200,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) gemm_tc_kernel(const __grid_con
                 const uint32_t st = base + s * stage_bytes;
                 const uint64_t da = sw128_desc(st), db0 = sw128_desc(st + a_bytes), db1 = sw128_desc(st + a_bytes + b_bytes);
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {  // 4 x K32 per 128-byte step; +32 bytes = +2 in the address field
+                for (int kk = 0; kk < 4; ++kk) {  // 4 x 32 bytes of K per 128-byte step: +2 in the address field
                     const uint32_t acc = (ks | kk) != 0;
                     mma_i8(taddr, da + 2 * kk, db0 + 2 * kk, idesc, acc);
                     mma_i8(taddr + a.nb, da + 2 * kk, db1 + 2 * kk, idesc, acc);
@@ -199,9 +217,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1) gemm_tc_kernel(const __grid_con
         const bool ok = mbar_wait(accum, 0, a.err, kErrMmaTimeout);
         tc_fence_after();
         if (ok) {
+            const uint32_t lane_addr = taddr + (static_cast<uint32_t>(quarter * 32) << 16);
             const float s0 = __fdiv_rn(a.act_max[0], 127.0f), s1 = __fdiv_rn(a.act_max[1], 127.0f);
             const float rs = row < a.n ? a.row_scale[row] : 0.f;
-            const uint32_t lane_addr = taddr + (static_cast<uint32_t>(quarter * 32) << 16);
             for (int c0 = 0; c0 < a.nb; c0 += 16) {
                 uint32_t p0[16], p1[16];
                 tmem_ld16(lane_addr + c0, p0);
@@ -225,6 +243,156 @@ __global__ void __launch_bounds__(kThreadsTc, 1) gemm_tc_kernel(const __grid_con
         tc_fence_after();
         tmem_dealloc(taddr, a.tmem_cols);
     }
+}
+
+// f16 weights, chunked accumulation; NB activation columns per CTA.
+constexpr int kChunkSteps = 4;
+template <int NB>
+__global__ void __launch_bounds__(kThreadsTc, 1) gemm_f16_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+    uint8_t *smem = smem_raw + (base - smem_u32(smem_raw));
+    constexpr uint32_t a_bytes = kTileM * kStepBytes, b_bytes = NB * kStepBytes;
+    constexpr uint32_t stage_bytes = a_bytes + 2 * b_bytes;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + a.stages * stage_bytes);
+    uint64_t *empty = full + a.stages;
+    uint64_t *tfull = empty + a.stages;  // [2] a tensor-memory slot holds a finished chunk
+    uint64_t *tfree = tfull + 2;         // [2] the epilogue has read a slot
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tfree + 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * kTileM, n0 = blockIdx.y * NB;
+    const int nchunks = (a.ksteps + kChunkSteps - 1) / kChunkSteps;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < a.stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int t = 0; t < 2; ++t) {
+            mbar_init(&tfull[t], 1);
+            mbar_init(&tfree[t], 4);  // one arrival per epilogue warp
+        }
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, a.tmem_cols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t taddr = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            pdl_wait_prior();
+            for (int ks = 0; ks < a.ksteps; ++ks) {
+                const int s = ks % a.stages;
+                if (ks >= a.stages && !mbar_wait(&empty[s], ((ks / a.stages) - 1) & 1, a.err, kErrBulkTimeout)) break;
+                const uint32_t st = base + s * stage_bytes;
+                mbar_arrive_expect_tx(&full[s], stage_bytes);
+                tma_2d(st, &maps.a, ks * kStepBytes, m0, &full[s]);
+                tma_2d(st + a_bytes, &maps.b0, ks * kStepBytes, n0, &full[s]);
+                tma_2d(st + a_bytes + b_bytes, &maps.b1, ks * kStepBytes, n0, &full[s]);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = instr_desc(1, 0, 0, kTileM, NB);  // f32 <- f16 x f16
+            bool ok = true;
+            for (int c = 0; c < nchunks && ok; ++c) {
+                const int slot = c & 1;
+                if (c >= 2 && !mbar_wait(&tfree[slot], ((c >> 1) - 1) & 1, a.err, kErrMmaTimeout)) break;
+                tc_fence_after();
+                const uint32_t d = taddr + slot * NB;
+                const int ks_end = min(a.ksteps, (c + 1) * kChunkSteps);
+                for (int ks = c * kChunkSteps; ks < ks_end; ++ks) {
+                    const int s = ks % a.stages;
+                    if (!mbar_wait(&full[s], (ks / a.stages) & 1, a.err, kErrBulkTimeout)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t st = base + s * stage_bytes;
+                    const uint64_t da = sw128_desc(st), db0 = sw128_desc(st + a_bytes), db1 = sw128_desc(st + a_bytes + b_bytes);
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        mma_f16(d, da + 2 * kk, db0 + 2 * kk, idesc, (ks != c * kChunkSteps) || kk != 0);
+                        mma_f16(d, da + 2 * kk, db1 + 2 * kk, idesc, 1);
+                    }
+                    mma_commit(&empty[s]);
+                }
+                mma_commit(&tfull[slot]);
+            }
+        }
+        __syncwarp();
+    } else {
+        const int quarter = warp & 3;
+        const int row = m0 + quarter * 32 + lane;
+        const uint32_t lane_addr = taddr + (static_cast<uint32_t>(quarter * 32) << 16);
+        float sum[NB];
+#pragma unroll
+        for (int i = 0; i < NB; ++i) sum[i] = 0.f;
+        bool ok = true;
+        for (int c = 0; c < nchunks; ++c) {
+            const int slot = c & 1;
+            if (!mbar_wait(&tfull[slot], (c >> 1) & 1, a.err, kErrMmaTimeout)) { ok = false; break; }
+            tc_fence_after();
+#pragma unroll
+            for (int c0 = 0; c0 < NB; c0 += 16) {
+                uint32_t p[16];
+                tmem_ld16(lane_addr + slot * NB + c0, p);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 16; ++i) sum[c0 + i] = __fadd_rn(sum[c0 + i], __uint_as_float(p[i]));
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tfree[slot]);
+        }
+        if (ok && row < a.n) {
+#pragma unroll
+            for (int i = 0; i < NB; ++i) {
+                const int col = n0 + i;
+                if (col < a.batch) a.y[static_cast<long long>(col) * a.y_stride + row] = __fmul_rn(sum[i], a.col_scale[col]);
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(taddr, a.tmem_cols);
+    }
+}
+
+// Activation rows for the f16 kernel: x[b, :] = 2^e[b] * (hi + lo), e chosen so that the
+// row's largest magnitude lies in [2^14, 2^15) (f16 hi/lo keep ~22 bits for
+// values down to ~2^-28 of it).  One CTA per row.
+__global__ void __launch_bounds__(256) split_rows_kernel(const float *x, int k, int x_stride, __half *hi, __half *lo,
+                                                         float *scale) {
+    __shared__ uint32_t red[8];
+    const float *src = x + static_cast<long long>(blockIdx.x) * x_stride;
+    uint32_t m = 0;
+    for (int j = threadIdx.x; j < k; j += blockDim.x) m = max(m, __float_as_uint(src[j]) & 0x7fffffffu);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    m = 0;
+    for (int i = 0; i < (blockDim.x >> 5); ++i) m = max(m, red[i]);
+    int e = 0;
+    if (m != 0 && m < 0x7f800000u) {
+        int ex = static_cast<int>(m >> 23) - 127;
+        if (m < 0x00800000u) ex = (31 - __clz(static_cast<int>(m))) - 149;
+        e = min(max(ex - 14, -126), 113);
+    }
+    const float s = __uint_as_float(static_cast<uint32_t>(127 - e) << 23);
+    __half *h = hi + static_cast<long long>(blockIdx.x) * k, *l = lo + static_cast<long long>(blockIdx.x) * k;
+    for (int j = threadIdx.x; j < k; j += blockDim.x) {
+        const float v = __fmul_rn(src[j], s);
+        const __half hv = __float2half_rn(v);
+        const float hf = __half2float(hv);
+        h[j] = hv;
+        l[j] = (__float_as_uint(hf) & 0x7fffffffu) < 0x7f800000u ? __float2half_rn(__fsub_rn(v, hf)) : __ushort_as_half(0);
+    }
+    if (threadIdx.x == 0) scale[blockIdx.x] = __uint_as_float(static_cast<uint32_t>(e + 127) << 23);
 }
 
 // ---- host side -------------------------------------------------------------
@@ -261,14 +429,21 @@ bool encode_kmajor(CUtensorMap &m, const void *ptr, long long row_bytes, int row
 
 bool gemm_tc_supported(int wt, int k, int n, int batch) {
     (void)n;
-    return wt == 3 && batch >= kTcMinBatch && k % 16 == 0;
+    return (wt == 3 || wt == 1) && batch >= kTcMinBatch && k % 16 == 0;
+}
+
+size_t gemm_tc_scratch_bytes(int wt, int k, int batch) {
+    if (wt != 1) return 0;
+    return ((static_cast<size_t>(batch) * k * 2 + 255) & ~size_t(255)) * 2 + static_cast<size_t>(batch) * 4;
 }
 
 cudaError_t launch_gemm_tc(const GemvRequest &r, const DeviceInfo &dev, cudaStream_t stream) {
     if (!gemm_tc_supported(r.wt, r.k, r.n, r.batch)) return cudaErrorNotSupported;
-    if ((reinterpret_cast<uintptr_t>(r.w) & 15) || (reinterpret_cast<uintptr_t>(r.q) & 15) || (r.q_comp & 15) ||
-        r.q_stride != r.k)
+    const bool i8 = r.wt == 3;
+    if (reinterpret_cast<uintptr_t>(r.w) & 15) return cudaErrorNotSupported;
+    if (i8 && ((reinterpret_cast<uintptr_t>(r.q) & 15) || (r.q_comp & 15) || r.q_stride != r.k))
         return cudaErrorNotSupported;
+    if (!i8 && (!r.split || r.split_bytes < gemm_tc_scratch_bytes(r.wt, r.k, r.batch))) return cudaErrorNotSupported;
     TcArgs a{};
     a.y = r.y;
     a.row_scale = r.row_scale;
@@ -278,10 +453,13 @@ cudaError_t launch_gemm_tc(const GemvRequest &r, const DeviceInfo &dev, cudaStre
     a.n = r.n;
     a.batch = r.batch;
     a.y_stride = r.y_stride;
-    a.nb = r.batch >= 256 ? 256 : (r.batch + 15) / 16 * 16;
-    a.ksteps = (r.k + kStepBytes - 1) / kStepBytes;
+    const int cap = i8 ? 256 : 128;  // the f16 epilogue keeps NB sums per thread in registers
+    a.nb = r.batch >= cap ? cap : (r.batch + 15) / 16 * 16;
+    if (!i8) a.nb = a.nb <= 16 ? 16 : a.nb <= 32 ? 32 : a.nb <= 64 ? 64 : 128;
+    const long long row_bytes = i8 ? r.k : 2ll * r.k;
+    a.ksteps = static_cast<int>((row_bytes + kStepBytes - 1) / kStepBytes);
     uint32_t cols = 32;
-    while (cols < static_cast<uint32_t>(2 * a.nb)) cols <<= 1;
+    while (cols < static_cast<uint32_t>(2 * a.nb)) cols <<= 1;  // two accumulators or two slots
     a.tmem_cols = cols;
     const size_t stage = static_cast<size_t>(kTileM) * kStepBytes + 2 * static_cast<size_t>(a.nb) * kStepBytes;
     const size_t budget = static_cast<size_t>(dev.smem_optin) - 1024 - 256;
@@ -291,17 +469,33 @@ cudaError_t launch_gemm_tc(const GemvRequest &r, const DeviceInfo &dev, cudaStre
     a.stages = stages;
     const size_t smem = 1024 + stages * stage + 256;
     TcMaps maps;
-    if (!encode_kmajor(maps.a, r.w, r.k, r.n, kTileM) || !encode_kmajor(maps.b0, r.q, r.k, r.batch, a.nb) ||
-        !encode_kmajor(maps.b1, r.q + r.q_comp, r.k, r.batch, a.nb))
+    const void *b0 = r.q, *b1 = r.q ? r.q + r.q_comp : nullptr;
+    if (!i8) {
+        // split the activation rows into f16 hi/lo (scratch: hi | lo | scales)
+        const size_t part = (static_cast<size_t>(r.batch) * r.k * 2 + 255) & ~size_t(255);
+        __half *hi = static_cast<__half *>(r.split);
+        __half *lo = reinterpret_cast<__half *>(static_cast<char *>(r.split) + part);
+        float *sc = reinterpret_cast<float *>(static_cast<char *>(r.split) + 2 * part);
+        split_rows_kernel<<<r.batch, 256, 0, stream>>>(r.x, r.k, r.x_stride, hi, lo, sc);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        b0 = hi;
+        b1 = lo;
+        a.col_scale = sc;
+    }
+    if (!encode_kmajor(maps.a, r.w, row_bytes, r.n, kTileM) || !encode_kmajor(maps.b0, b0, row_bytes, r.batch, a.nb) ||
+        !encode_kmajor(maps.b1, b1, row_bytes, r.batch, a.nb))
         return cudaErrorNotSupported;
-    auto kern = gemm_tc_kernel<kI8>;
-    static int configured[64] = {0};
+    void (*kern)(TcMaps, TcArgs) = gemm_i8_kernel;
+    if (!i8) kern = a.nb == 16 ? gemm_f16_kernel<16> : a.nb == 32 ? gemm_f16_kernel<32> : a.nb == 64 ? gemm_f16_kernel<64> : gemm_f16_kernel<128>;
+    static int configured[5][64] = {{0}};
+    const int ki = i8 ? 0 : a.nb == 16 ? 1 : a.nb == 32 ? 2 : a.nb == 64 ? 3 : 4;
     int devno = 0;
     cudaGetDevice(&devno);
-    if (devno < 0 || devno >= 64 || configured[devno] < static_cast<int>(smem)) {
+    if (devno < 0 || devno >= 64 || configured[ki][devno] < static_cast<int>(smem)) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
-        if (devno >= 0 && devno < 64) configured[devno] = static_cast<int>(smem);
+        if (devno >= 0 && devno < 64) configured[ki][devno] = static_cast<int>(smem);
     }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((r.n + kTileM - 1) / kTileM, (r.batch + a.nb - 1) / a.nb);

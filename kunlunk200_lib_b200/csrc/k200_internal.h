@@ -31,6 +31,8 @@ struct GemvRequest {
     void *fixup = nullptr;         // Kernel-owned scratch of the tensor-core Q4_0 GEMV (counters
     size_t fixup_bytes = 0;        // zeroed at allocation, partial sums), see q4_mma_scratch_bytes
     bool tensor_cores = true;      // batched shapes may take the tcgen05 GEMM (KUNLUN_TC=0: never)
+    void *split = nullptr;         // Kernel-owned scratch for the GEMM's split activations
+    size_t split_bytes = 0;        // (gemm_tc_scratch_bytes)
 };
 
 // Streaming GEMV launcher (handles any batch by column groups).
@@ -44,9 +46,11 @@ cudaError_t launch_gemv(const GemvRequest &r, const DeviceInfo &dev, cudaStream_
 size_t q4_mma_scratch_bytes(int k, int n, int batch, const DeviceInfo &dev);
 
 // tcgen05 GEMM for batches of columns (gemm_tc.cu): rowwise-int8 with the
-// activation components already quantised (GemvRequest::q).
+// activation components already quantised (GemvRequest::q), and f16 weights
+// with f32 activations (which need gemm_tc_scratch_bytes of scratch).
 constexpr int kTcMinBatch = 4;
 bool gemm_tc_supported(int wt, int k, int n, int batch);
+size_t gemm_tc_scratch_bytes(int wt, int k, int batch);
 cudaError_t launch_gemm_tc(const GemvRequest &r, const DeviceInfo &dev, cudaStream_t stream);
 cudaError_t launch_q4_mma_gemv(const GemvRequest &r, const DeviceInfo &dev, cudaStream_t stream);
 bool gemv_fast_path_ok(int wt, const void *w, const void *x, const void *y, int k, long long row_bytes);

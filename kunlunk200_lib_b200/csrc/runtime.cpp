@@ -260,6 +260,8 @@ struct Kernel::Impl {
     size_t alias_size = 0;
     void *fixup = nullptr;   // tensor-core Q4_0 GEMV: tile counters (zeroed) + partial sums
     size_t fixup_size = 0;
+    void *split = nullptr;   // tensor-core GEMM: activations split into f16 hi/lo
+    size_t split_size = 0;
 };
 
 Kernel::Kernel() : impl_(new Impl{}) {}
@@ -273,6 +275,7 @@ Kernel::~Kernel() {
         release(s.id, s.params, 256);
         release(s.id, s.alias, s.alias_size);
         release(s.id, s.fixup, s.fixup_size);
+        release(s.id, s.split, s.split_size);
     }
     delete impl_;
 }
@@ -351,6 +354,14 @@ void matmul(Kernel &kernel, int id, void *y, const void *w, const void *x, int k
             }
             r.fixup = s.fixup;
             r.fixup_bytes = s.fixup_size;
+        }
+        const size_t split = d.tensor_cores && k200::gemm_tc_supported((int)type, k, n, batch)
+                                 ? k200::gemm_tc_scratch_bytes((int)type, k, batch)
+                                 : 0;
+        if (split) {
+            grow(s, s.split, s.split_size, split);
+            r.split = s.split;
+            r.split_bytes = s.split_size;
         }
     }
     check((int)k200::launch_gemv(r, d.info, d.stream));
