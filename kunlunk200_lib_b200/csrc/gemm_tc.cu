@@ -32,6 +32,11 @@
 //    other slot fills.  The reference computes these products in FP32
 //    (kernels/kunlun-matvec.xpu); the difference is the ~2^-22 split plus
 //    the order of the f32 sums.
+//  * Q4_0 weights (the same kernel with a second weight operand): the blocks
+//    are first expanded into f16 pairs W' = d*(q-8) = hi + lo (exact: hi =
+//    f16(d*(q-8)), lo = fma(d, q-8, -hi), the residual has at most 3
+//    significant bits), then three products are accumulated per K step:
+//    hi*x_hi + hi*x_lo + lo*x_hi (lo*x_lo is below 2^-21 of the term).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -51,6 +56,7 @@ constexpr int kThreadsTc = 192;   // 6 warps: TMA, MMA, 4 x epilogue
 
 struct TcMaps {
     CUtensorMap a;    // weights [n][k] (bytes)
+    CUtensorMap a1;   // second weight operand (the lo half of split weights)
     CUtensorMap b0;   // activation operand 0 [batch][k]
     CUtensorMap b1;   // activation operand 1 [batch][k]
 };
@@ -247,13 +253,15 @@ __global__ void __launch_bounds__(kThreadsTc, 1) gemm_i8_kernel(const __grid_con
 
 // f16 weights, chunked accumulation; NB activation columns per CTA.
 constexpr int kChunkSteps = 4;
-template <int NB>
+template <int NB, bool SPLITW>
 __global__ void __launch_bounds__(kThreadsTc, 1) gemm_f16_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
     uint8_t *smem = smem_raw + (base - smem_u32(smem_raw));
+    // stage: [A 128 x 128 B][A1 (split weights)][B0 NB x 128 B][B1 NB x 128 B]
     constexpr uint32_t a_bytes = kTileM * kStepBytes, b_bytes = NB * kStepBytes;
-    constexpr uint32_t stage_bytes = a_bytes + 2 * b_bytes;
+    constexpr uint32_t a_total = SPLITW ? 2 * a_bytes : a_bytes;
+    constexpr uint32_t stage_bytes = a_total + 2 * b_bytes;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + a.stages * stage_bytes);
     uint64_t *empty = full + a.stages;
     uint64_t *tfull = empty + a.stages;  // [2] a tensor-memory slot holds a finished chunk
@@ -290,8 +298,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1) gemm_f16_kernel(const __grid_co
                 const uint32_t st = base + s * stage_bytes;
                 mbar_arrive_expect_tx(&full[s], stage_bytes);
                 tma_2d(st, &maps.a, ks * kStepBytes, m0, &full[s]);
-                tma_2d(st + a_bytes, &maps.b0, ks * kStepBytes, n0, &full[s]);
-                tma_2d(st + a_bytes + b_bytes, &maps.b1, ks * kStepBytes, n0, &full[s]);
+                if constexpr (SPLITW) tma_2d(st + a_bytes, &maps.a1, ks * kStepBytes, m0, &full[s]);
+                tma_2d(st + a_total, &maps.b0, ks * kStepBytes, n0, &full[s]);
+                tma_2d(st + a_total + b_bytes, &maps.b1, ks * kStepBytes, n0, &full[s]);
             }
         }
         __syncwarp();
@@ -310,11 +319,13 @@ __global__ void __launch_bounds__(kThreadsTc, 1) gemm_f16_kernel(const __grid_co
                     if (!mbar_wait(&full[s], (ks / a.stages) & 1, a.err, kErrBulkTimeout)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t st = base + s * stage_bytes;
-                    const uint64_t da = sw128_desc(st), db0 = sw128_desc(st + a_bytes), db1 = sw128_desc(st + a_bytes + b_bytes);
+                    const uint64_t da = sw128_desc(st), da1 = sw128_desc(st + a_bytes);
+                    const uint64_t db0 = sw128_desc(st + a_total), db1 = sw128_desc(st + a_total + b_bytes);
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
                         mma_f16(d, da + 2 * kk, db0 + 2 * kk, idesc, (ks != c * kChunkSteps) || kk != 0);
                         mma_f16(d, da + 2 * kk, db1 + 2 * kk, idesc, 1);
+                        if constexpr (SPLITW) mma_f16(d, da1 + 2 * kk, db0 + 2 * kk, idesc, 1);
                     }
                     mma_commit(&empty[s]);
                 }
@@ -359,6 +370,46 @@ __global__ void __launch_bounds__(kThreadsTc, 1) gemm_f16_kernel(const __grid_co
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(taddr, a.tmem_cols);
+    }
+}
+
+// Q4_0 rows -> f16 hi/lo halves of W' = d*(q-8), row-major [rows][k]; one
+// thread per 32-element block (element j < 16: low nibble of byte j, j >= 16:
+// high nibble of byte j-16, as kernels/kunlun-matvec.xpu:51-59 decodes).
+__global__ void __launch_bounds__(256) dequant_q4_split_kernel(const uint8_t *q4, long long row_bytes, int k, int rows,
+                                                               __half *hi, __half *lo) {
+    const int blocks = k >> 5;
+    const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= static_cast<long long>(rows) * blocks) return;
+    const int r = static_cast<int>(idx / blocks), b = static_cast<int>(idx - static_cast<long long>(r) * blocks);
+    const uint8_t *blk = q4 + r * row_bytes + 18ll * b;
+    const uint16_t dbits = static_cast<uint16_t>(blk[0] | (blk[1] << 8));
+    const __half2 d2 = __halves2half2(__ushort_as_half(dbits), __ushort_as_half(dbits));
+    uint32_t qs[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        qs[i] = static_cast<uint32_t>(blk[2 + 4 * i]) | (static_cast<uint32_t>(blk[3 + 4 * i]) << 8) |
+                (static_cast<uint32_t>(blk[4 + 4 * i]) << 16) | (static_cast<uint32_t>(blk[5 + 4 * i]) << 24);
+    uint32_t h[16], l[16];
+#pragma unroll
+    for (int e = 0; e < 32; e += 2) {
+        // elements e, e+1 of the block
+        const int b0 = e & 15;                     // byte index
+        const int sh = e < 16 ? 0 : 4;             // nibble
+        const int v0 = ((qs[b0 >> 2] >> (8 * (b0 & 3) + sh)) & 15) - 8;
+        const int v1 = ((qs[(b0 + 1) >> 2] >> (8 * ((b0 + 1) & 3) + sh)) & 15) - 8;
+        const __half2 q2 = __halves2half2(__int2half_rn(v0), __int2half_rn(v1));
+        const __half2 hv = __hmul2(d2, q2);
+        const __half2 lv = __hfma2(d2, q2, __hneg2(hv));
+        h[e >> 1] = *reinterpret_cast<const uint32_t *>(&hv);
+        l[e >> 1] = *reinterpret_cast<const uint32_t *>(&lv);
+    }
+    uint4 *ho = reinterpret_cast<uint4 *>(hi + static_cast<long long>(r) * k + 32ll * b);
+    uint4 *lo4 = reinterpret_cast<uint4 *>(lo + static_cast<long long>(r) * k + 32ll * b);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        ho[i] = make_uint4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
+        lo4[i] = make_uint4(l[4 * i], l[4 * i + 1], l[4 * i + 2], l[4 * i + 3]);
     }
 }
 
@@ -429,21 +480,29 @@ bool encode_kmajor(CUtensorMap &m, const void *ptr, long long row_bytes, int row
 
 bool gemm_tc_supported(int wt, int k, int n, int batch) {
     (void)n;
-    return (wt == 3 || wt == 1) && batch >= kTcMinBatch && k % 16 == 0;
+    if (k % 16) return false;
+    if (wt == 3 || wt == 1) return batch >= kTcMinBatch;
+    return wt == 2 && batch >= kTcMinBatchQ4;
 }
 
-size_t gemm_tc_scratch_bytes(int wt, int k, int batch) {
-    if (wt != 1) return 0;
-    return ((static_cast<size_t>(batch) * k * 2 + 255) & ~size_t(255)) * 2 + static_cast<size_t>(batch) * 4;
+namespace {
+size_t align256(size_t b) { return (b + 255) & ~size_t(255); }
+}  // namespace
+
+size_t gemm_tc_scratch_bytes(int wt, int k, int n, int batch) {
+    if (wt != 1 && wt != 2) return 0;
+    size_t bytes = 2 * align256(static_cast<size_t>(batch) * k * 2) + align256(static_cast<size_t>(batch) * 4);
+    if (wt == 2) bytes += 2 * align256(static_cast<size_t>(n) * k * 2);  // expanded weights, hi and lo
+    return bytes;
 }
 
 cudaError_t launch_gemm_tc(const GemvRequest &r, const DeviceInfo &dev, cudaStream_t stream) {
     if (!gemm_tc_supported(r.wt, r.k, r.n, r.batch)) return cudaErrorNotSupported;
-    const bool i8 = r.wt == 3;
+    const bool i8 = r.wt == 3, q4 = r.wt == 2;
     if (reinterpret_cast<uintptr_t>(r.w) & 15) return cudaErrorNotSupported;
     if (i8 && ((reinterpret_cast<uintptr_t>(r.q) & 15) || (r.q_comp & 15) || r.q_stride != r.k))
         return cudaErrorNotSupported;
-    if (!i8 && (!r.split || r.split_bytes < gemm_tc_scratch_bytes(r.wt, r.k, r.batch))) return cudaErrorNotSupported;
+    if (!i8 && (!r.split || r.split_bytes < gemm_tc_scratch_bytes(r.wt, r.k, r.n, r.batch))) return cudaErrorNotSupported;
     TcArgs a{};
     a.y = r.y;
     a.row_scale = r.row_scale;
@@ -461,7 +520,7 @@ cudaError_t launch_gemm_tc(const GemvRequest &r, const DeviceInfo &dev, cudaStre
     uint32_t cols = 32;
     while (cols < static_cast<uint32_t>(2 * a.nb)) cols <<= 1;  // two accumulators or two slots
     a.tmem_cols = cols;
-    const size_t stage = static_cast<size_t>(kTileM) * kStepBytes + 2 * static_cast<size_t>(a.nb) * kStepBytes;
+    const size_t stage = static_cast<size_t>(kTileM) * kStepBytes * (q4 ? 2 : 1) + 2 * static_cast<size_t>(a.nb) * kStepBytes;
     const size_t budget = static_cast<size_t>(dev.smem_optin) - 1024 - 256;
     int stages = static_cast<int>(budget / stage);
     if (stages > 6) stages = 6;
@@ -469,27 +528,47 @@ cudaError_t launch_gemm_tc(const GemvRequest &r, const DeviceInfo &dev, cudaStre
     a.stages = stages;
     const size_t smem = 1024 + stages * stage + 256;
     TcMaps maps;
-    const void *b0 = r.q, *b1 = r.q ? r.q + r.q_comp : nullptr;
+    const void *w0 = r.w, *w1 = r.w, *b0 = r.q, *b1 = r.q ? r.q + r.q_comp : nullptr;
     if (!i8) {
-        // split the activation rows into f16 hi/lo (scratch: hi | lo | scales)
-        const size_t part = (static_cast<size_t>(r.batch) * r.k * 2 + 255) & ~size_t(255);
-        __half *hi = static_cast<__half *>(r.split);
-        __half *lo = reinterpret_cast<__half *>(static_cast<char *>(r.split) + part);
-        float *sc = reinterpret_cast<float *>(static_cast<char *>(r.split) + 2 * part);
+        // split the activation rows into f16 hi/lo (scratch: hi | lo | scales | expanded weights)
+        const size_t part = align256(static_cast<size_t>(r.batch) * r.k * 2);
+        char *base = static_cast<char *>(r.split);
+        __half *hi = reinterpret_cast<__half *>(base), *lo = reinterpret_cast<__half *>(base + part);
+        float *sc = reinterpret_cast<float *>(base + 2 * part);
         split_rows_kernel<<<r.batch, 256, 0, stream>>>(r.x, r.k, r.x_stride, hi, lo, sc);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
         b0 = hi;
         b1 = lo;
         a.col_scale = sc;
+        if (q4) {
+            char *wbase = base + 2 * part + align256(static_cast<size_t>(r.batch) * 4);
+            const size_t wpart = align256(static_cast<size_t>(r.n) * r.k * 2);
+            __half *whi = reinterpret_cast<__half *>(wbase), *wlo = reinterpret_cast<__half *>(wbase + wpart);
+            const long long blocks = static_cast<long long>(r.n) * (r.k / 32);
+            dequant_q4_split_kernel<<<static_cast<unsigned>((blocks + 255) / 256), 256, 0, stream>>>(
+                static_cast<const uint8_t *>(r.w), static_cast<long long>(r.k / 32) * 18, r.k, r.n, whi, wlo);
+            e = cudaGetLastError();
+            if (e != cudaSuccess) return e;
+            w0 = whi;
+            w1 = wlo;
+        }
     }
-    if (!encode_kmajor(maps.a, r.w, row_bytes, r.n, kTileM) || !encode_kmajor(maps.b0, b0, row_bytes, r.batch, a.nb) ||
-        !encode_kmajor(maps.b1, b1, row_bytes, r.batch, a.nb))
+    if (!encode_kmajor(maps.a, w0, row_bytes, r.n, kTileM) || !encode_kmajor(maps.a1, w1, row_bytes, r.n, kTileM) ||
+        !encode_kmajor(maps.b0, b0, row_bytes, r.batch, a.nb) || !encode_kmajor(maps.b1, b1, row_bytes, r.batch, a.nb))
         return cudaErrorNotSupported;
     void (*kern)(TcMaps, TcArgs) = gemm_i8_kernel;
-    if (!i8) kern = a.nb == 16 ? gemm_f16_kernel<16> : a.nb == 32 ? gemm_f16_kernel<32> : a.nb == 64 ? gemm_f16_kernel<64> : gemm_f16_kernel<128>;
-    static int configured[5][64] = {{0}};
-    const int ki = i8 ? 0 : a.nb == 16 ? 1 : a.nb == 32 ? 2 : a.nb == 64 ? 3 : 4;
+    int ki = 0;
+    if (!i8) {
+        const int which = a.nb == 16 ? 0 : a.nb == 32 ? 1 : a.nb == 64 ? 2 : 3;
+        static void (*const f16k[4])(TcMaps, TcArgs) = {gemm_f16_kernel<16, false>, gemm_f16_kernel<32, false>,
+                                                          gemm_f16_kernel<64, false>, gemm_f16_kernel<128, false>};
+        static void (*const q4k[4])(TcMaps, TcArgs) = {gemm_f16_kernel<16, true>, gemm_f16_kernel<32, true>,
+                                                         gemm_f16_kernel<64, true>, gemm_f16_kernel<128, true>};
+        kern = q4 ? q4k[which] : f16k[which];
+        ki = 1 + which + (q4 ? 4 : 0);
+    }
+    static int configured[9][64] = {{0}};
     int devno = 0;
     cudaGetDevice(&devno);
     if (devno < 0 || devno >= 64 || configured[ki][devno] < static_cast<int>(smem)) {

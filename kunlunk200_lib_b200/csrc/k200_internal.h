@@ -46,11 +46,13 @@ cudaError_t launch_gemv(const GemvRequest &r, const DeviceInfo &dev, cudaStream_
 size_t q4_mma_scratch_bytes(int k, int n, int batch, const DeviceInfo &dev);
 
 // tcgen05 GEMM for batches of columns (gemm_tc.cu): rowwise-int8 with the
-// activation components already quantised (GemvRequest::q), and f16 weights
-// with f32 activations (which need gemm_tc_scratch_bytes of scratch).
+// activation components already quantised (GemvRequest::q), and f16 and
+// q4_0 weights with f32 activations (which need gemm_tc_scratch_bytes of
+// scratch in GemvRequest::split).
 constexpr int kTcMinBatch = 4;
+constexpr int kTcMinBatchQ4 = 8;   // q4_0: the weights are expanded to f16 hi/lo first
 bool gemm_tc_supported(int wt, int k, int n, int batch);
-size_t gemm_tc_scratch_bytes(int wt, int k, int batch);
+size_t gemm_tc_scratch_bytes(int wt, int k, int n, int batch);
 cudaError_t launch_gemm_tc(const GemvRequest &r, const DeviceInfo &dev, cudaStream_t stream);
 cudaError_t launch_q4_mma_gemv(const GemvRequest &r, const DeviceInfo &dev, cudaStream_t stream);
 bool gemv_fast_path_ok(int wt, const void *w, const void *x, const void *y, int k, long long row_bytes);

@@ -356,7 +356,7 @@ void matmul(Kernel &kernel, int id, void *y, const void *w, const void *x, int k
             r.fixup_bytes = s.fixup_size;
         }
         const size_t split = d.tensor_cores && k200::gemm_tc_supported((int)type, k, n, batch)
-                                 ? k200::gemm_tc_scratch_bytes((int)type, k, batch)
+                                 ? k200::gemm_tc_scratch_bytes((int)type, k, n, batch)
                                  : 0;
         if (split) {
             grow(s, s.split, s.split_size, split);

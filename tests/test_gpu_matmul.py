@@ -103,6 +103,18 @@ def test_q4_0_matches_fp64_gold(K, O, gpu, k, n, batch):
     _check_float(y, gold)
 
 
+@pytest.mark.parametrize("k,n,batch", [(4096, 1024, 32), (4096, 512, 128), (1056, 300, 300)])
+def test_q4_0_batched_tensor_cores(K, O, gpu, k, n, batch):
+    """Config 2 class (batched q4_0 on the tensor cores after the f16 hi/lo
+    weight expansion), held to the reference's q4_0 bar (library-bench tol
+    1e-3) and an NMSE far below it."""
+    q4, x = _q4_case(O, k, n, batch)
+    y = _device_matmul(K, K.Q4_0, q4, x, k, n, batch)
+    gold = O.matmul_gold(q4, O.WT_Q4_0, x, k, n, batch)
+    _check_float(y, gold, tol=TOL_F16_TC)
+    assert np.sum((y - gold) ** 2) / np.sum(gold ** 2) < 1e-8
+
+
 def test_q4_0_library_bench_closed_form(K, O, gpu):
     """bench/library-bench.cpp:89-101 inputs at the verify.sh shape (256, 65, 4)."""
     k, n, b = 256, 65, 4
