@@ -32,11 +32,21 @@
 //    other slot fills.  The reference computes these products in FP32
 //    (kernels/kunlun-matvec.xpu); the difference is the ~2^-22 split plus
 //    the order of the f32 sums.
-//  * Q4_0 weights (the same kernel with a second weight operand): the blocks
-//    are first expanded into f16 pairs W' = d*(q-8) = hi + lo (exact: hi =
-//    f16(d*(q-8)), lo = fma(d, q-8, -hi), the residual has at most 3
-//    significant bits), then three products are accumulated per K step:
-//    hi*x_hi + hi*x_lo + lo*x_hi (lo*x_lo is below 2^-21 of the term).
+//  * Q4_0 weights (gemm_q4_kernel): four dequantiser warps, one weight row
+//    per thread, read each K step's two blocks (36 bytes) straight from
+//    global memory and write W' = d*(q-8) into shared memory as exact f16
+//    hi + lo halves (hi = f16(d*(q-8)), lo = fma(d, q-8, -hi): the residual
+//    has at most 3 significant bits) in the swizzled layout the MMA reads.
+//    The raw blocks arrive by TMA in boxes of 128 rows x 144 bytes (four
+//    K steps) through a ring of 3-4 slots filled by a dedicated producer
+//    warp; each dequantiser reads its row's 144 bytes with nine
+//    conflict-free 16-byte shared loads.  (Per-thread global loads of the
+//    36-byte row pieces touch 32 sectors per instruction and saturate L1.)
+//    Three products per K step: hi*x_hi + hi*x_lo + lo*x_hi (lo*x_lo is
+//    below 2^-21 of the term).  Each 16-byte chunk holds one decoded nibble
+//    word in the order the decode produces, and the activations are split
+//    into the same permuted K order (q4_pos below), so the sums are those of
+//    the natural order.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -56,12 +66,13 @@ constexpr int kThreadsTc = 192;   // 6 warps: TMA, MMA, 4 x epilogue
 
 struct TcMaps {
     CUtensorMap a;    // weights [n][k] (bytes)
-    CUtensorMap a1;   // second weight operand (the lo half of split weights)
     CUtensorMap b0;   // activation operand 0 [batch][k]
     CUtensorMap b1;   // activation operand 1 [batch][k]
 };
 
 struct TcArgs {
+    const uint8_t *w;        // q4_0: weight rows (read by the dequantisers)
+    long long row_bytes;     // q4_0: bytes per weight row
     float *y;
     const float *row_scale;  // rowwise-int8: per weight row scale
     const float *act_max;    // rowwise-int8: {max0, max1}
@@ -72,6 +83,7 @@ struct TcArgs {
     int stages;
     int ksteps;
     uint32_t tmem_cols;      // allocated tensor-memory columns (power of two >= 32)
+    int raw_slots;           // q4: raw weight boxes in flight
 };
 
 // ---- tcgen05 primitives ----------------------------------------------------
@@ -253,14 +265,14 @@ __global__ void __launch_bounds__(kThreadsTc, 1) gemm_i8_kernel(const __grid_con
 
 // f16 weights, chunked accumulation; NB activation columns per CTA.
 constexpr int kChunkSteps = 4;
-template <int NB, bool SPLITW>
+template <int NB>
 __global__ void __launch_bounds__(kThreadsTc, 1) gemm_f16_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
     uint8_t *smem = smem_raw + (base - smem_u32(smem_raw));
-    // stage: [A 128 x 128 B][A1 (split weights)][B0 NB x 128 B][B1 NB x 128 B]
+    // stage: [A 128 x 128 B][B0 NB x 128 B][B1 NB x 128 B]
     constexpr uint32_t a_bytes = kTileM * kStepBytes, b_bytes = NB * kStepBytes;
-    constexpr uint32_t a_total = SPLITW ? 2 * a_bytes : a_bytes;
+    constexpr uint32_t a_total = a_bytes;
     constexpr uint32_t stage_bytes = a_total + 2 * b_bytes;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + a.stages * stage_bytes);
     uint64_t *empty = full + a.stages;
@@ -298,7 +310,6 @@ __global__ void __launch_bounds__(kThreadsTc, 1) gemm_f16_kernel(const __grid_co
                 const uint32_t st = base + s * stage_bytes;
                 mbar_arrive_expect_tx(&full[s], stage_bytes);
                 tma_2d(st, &maps.a, ks * kStepBytes, m0, &full[s]);
-                if constexpr (SPLITW) tma_2d(st + a_bytes, &maps.a1, ks * kStepBytes, m0, &full[s]);
                 tma_2d(st + a_total, &maps.b0, ks * kStepBytes, n0, &full[s]);
                 tma_2d(st + a_total + b_bytes, &maps.b1, ks * kStepBytes, n0, &full[s]);
             }
@@ -319,13 +330,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1) gemm_f16_kernel(const __grid_co
                     if (!mbar_wait(&full[s], (ks / a.stages) & 1, a.err, kErrBulkTimeout)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t st = base + s * stage_bytes;
-                    const uint64_t da = sw128_desc(st), da1 = sw128_desc(st + a_bytes);
+                    const uint64_t da = sw128_desc(st);
                     const uint64_t db0 = sw128_desc(st + a_total), db1 = sw128_desc(st + a_total + b_bytes);
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
                         mma_f16(d, da + 2 * kk, db0 + 2 * kk, idesc, (ks != c * kChunkSteps) || kk != 0);
                         mma_f16(d, da + 2 * kk, db1 + 2 * kk, idesc, 1);
-                        if constexpr (SPLITW) mma_f16(d, da1 + 2 * kk, db0 + 2 * kk, idesc, 1);
                     }
                     mma_commit(&empty[s]);
                 }
@@ -373,51 +383,249 @@ __global__ void __launch_bounds__(kThreadsTc, 1) gemm_f16_kernel(const __grid_co
     }
 }
 
-// Q4_0 rows -> f16 hi/lo halves of W' = d*(q-8), row-major [rows][k]; one
-// thread per 32-element block (element j < 16: low nibble of byte j, j >= 16:
-// high nibble of byte j-16, as kernels/kunlun-matvec.xpu:51-59 decodes).
-__global__ void __launch_bounds__(256) dequant_q4_split_kernel(const uint8_t *q4, long long row_bytes, int k, int rows,
-                                                               __half *hi, __half *lo) {
-    const int blocks = k >> 5;
-    const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (idx >= static_cast<long long>(rows) * blocks) return;
-    const int r = static_cast<int>(idx / blocks), b = static_cast<int>(idx - static_cast<long long>(r) * blocks);
-    const uint8_t *blk = q4 + r * row_bytes + 18ll * b;
-    const uint16_t dbits = static_cast<uint16_t>(blk[0] | (blk[1] << 8));
-    const __half2 d2 = __halves2half2(__ushort_as_half(dbits), __ushort_as_half(dbits));
-    uint32_t qs[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-        qs[i] = static_cast<uint32_t>(blk[2 + 4 * i]) | (static_cast<uint32_t>(blk[3 + 4 * i]) << 8) |
-                (static_cast<uint32_t>(blk[4 + 4 * i]) << 16) | (static_cast<uint32_t>(blk[5 + 4 * i]) << 24);
-    uint32_t h[16], l[16];
-#pragma unroll
-    for (int e = 0; e < 32; e += 2) {
-        // elements e, e+1 of the block
-        const int b0 = e & 15;                     // byte index
-        const int sh = e < 16 ? 0 : 4;             // nibble
-        const int v0 = ((qs[b0 >> 2] >> (8 * (b0 & 3) + sh)) & 15) - 8;
-        const int v1 = ((qs[(b0 + 1) >> 2] >> (8 * ((b0 + 1) & 3) + sh)) & 15) - 8;
-        const __half2 q2 = __halves2half2(__int2half_rn(v0), __int2half_rn(v1));
-        const __half2 hv = __hmul2(d2, q2);
-        const __half2 lv = __hfma2(d2, q2, __hneg2(hv));
-        h[e >> 1] = *reinterpret_cast<const uint32_t *>(&hv);
-        l[e >> 1] = *reinterpret_cast<const uint32_t *>(&lv);
-    }
-    uint4 *ho = reinterpret_cast<uint4 *>(hi + static_cast<long long>(r) * k + 32ll * b);
-    uint4 *lo4 = reinterpret_cast<uint4 *>(lo + static_cast<long long>(r) * k + 32ll * b);
+// ---- q4_0 with in-kernel dequantisation -------------------------------------
+constexpr int kThreadsQ4 = 352;  // x TMA, MMA, 4 x epilogue, 4 x dequantiser, weight TMA
+constexpr int kRawRow = 144;     // bytes of one weight row per raw box: 4 K steps of 2 blocks
+constexpr int kRawBox = kTileM * kRawRow;  // 18 KB
+constexpr int kBarBytesQ4 = 1024;          // mbarriers and the TMEM slot
+
+// Position of element e (0..31) of a block inside the block's 32 K positions
+// after dequantisation: 16-byte chunk q (nibble bytes 4q..4q+3) holds
+// elements 4q, 4q+2, 16+4q, 18+4q, 4q+1, 4q+3, 17+4q, 19+4q.
+__host__ __device__ constexpr int q4_pos(int e) {
+    const int hi = e >= 16, j = e & 15, q = j >> 2, b = j & 3;
+    return 8 * q + ((b & 1) ? 4 : 0) + (hi ? 2 : 0) + (b >> 1);
+}
+
+// One nibble word (bytes b0..b3) -> the chunk's 8 values as f16 pairs of
+// (v - 8): {lo(b0), lo(b2)}, {hi(b0), hi(b2)}, {lo(b1), lo(b3)}, {hi(b1), hi(b3)}.
+__device__ __forceinline__ void q4_word_f16(uint32_t w, uint32_t (&t)[4]) {
+    const uint32_t m = 0x64006400u;
+    uint32_t a0, a1, a2, a3;
+    const uint32_t w8 = w >> 8;
+    asm("lop3.b32 %0, %1, 0x000F000F, %2, 0xEA;" : "=r"(a0) : "r"(w), "r"(m));
+    asm("lop3.b32 %0, %1, 0x00F000F0, %2, 0xEA;" : "=r"(a1) : "r"(w), "r"(m));
+    asm("lop3.b32 %0, %1, 0x000F000F, %2, 0xEA;" : "=r"(a2) : "r"(w8), "r"(m));
+    asm("lop3.b32 %0, %1, 0x00F000F0, %2, 0xEA;" : "=r"(a3) : "r"(w8), "r"(m));
+    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(t[0]) : "r"(a0), "r"(0xE408E408u));                  // 1024+v - 1032
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(t[1]) : "r"(a1), "r"(0x2C002C00u), "r"(0xD480D480u));  // /16 - 72
+    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(t[2]) : "r"(a2), "r"(0xE408E408u));
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(t[3]) : "r"(a3), "r"(0x2C002C00u), "r"(0xD480D480u));
+}
+
+// d*(v-8) for 8 values -> hi and lo chunks
+__device__ __forceinline__ void q4_chunk(uint32_t w, uint32_t d2, uint4 &hi, uint4 &lo) {
+    uint32_t t[4], h[4], l[4];
+    q4_word_f16(w, t);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        ho[i] = make_uint4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
-        lo4[i] = make_uint4(l[4 * i], l[4 * i + 1], l[4 * i + 2], l[4 * i + 3]);
+        asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(h[i]) : "r"(d2), "r"(t[i]));
+        asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(l[i]) : "r"(d2), "r"(t[i]), "r"(h[i] ^ 0x80008000u));
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+__device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+template <int NB>
+__global__ void __launch_bounds__(kThreadsQ4, 1) gemm_q4_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+    uint8_t *smem = smem_raw + (base - smem_u32(smem_raw));
+    // stage: [W hi 128 x 128 B][W lo 128 x 128 B][x hi NB x 128 B][x lo NB x 128 B]
+    constexpr uint32_t a_bytes = kTileM * kStepBytes, b_bytes = NB * kStepBytes;
+    constexpr uint32_t stage_bytes = 2 * a_bytes + 2 * b_bytes;
+    uint64_t *full_x = reinterpret_cast<uint64_t *>(smem + a.stages * stage_bytes);
+    uint64_t *full_w = full_x + a.stages;
+    uint64_t *empty = full_w + a.stages;
+    uint64_t *tfull = empty + a.stages;
+    uint64_t *tfree = tfull + 2;
+    uint64_t *full_r = tfree + 2;         // raw box landed (TMA)
+    uint64_t *empty_r = full_r + a.raw_slots;  // raw box read by all 128 dequantisers
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(empty_r + a.raw_slots);
+    const uint32_t raw_u = base + a.stages * stage_bytes + kBarBytesQ4;  // raw ring [slot][row][144 B]
+    const int nbox = a.ksteps / 4;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * kTileM, n0 = blockIdx.y * NB;
+    const int nchunks = (a.ksteps + kChunkSteps - 1) / kChunkSteps;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < a.stages; ++s) {
+            mbar_init(&full_x[s], 1);
+            mbar_init(&full_w[s], 128);  // one arrival per dequantiser thread
+            mbar_init(&empty[s], 1);
+        }
+        for (int t = 0; t < 2; ++t) {
+            mbar_init(&tfull[t], 1);
+            mbar_init(&tfree[t], 4);
+        }
+        for (int r = 0; r < a.raw_slots; ++r) {
+            mbar_init(&full_r[r], 1);
+            mbar_init(&empty_r[r], 128);
+        }
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, a.tmem_cols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t taddr = *tmem_slot;
+
+    if (warp == 10) {
+        // ---------------- raw weight boxes by TMA ----------------
+        if (lane == 0) {
+            pdl_wait_prior();
+            for (int rb = 0; rb < nbox; ++rb) {
+                const int rs = rb % a.raw_slots;
+                if (rb >= a.raw_slots &&
+                    !mbar_wait(&empty_r[rs], ((rb / a.raw_slots) - 1) & 1, a.err, kErrBulkTimeout))
+                    break;
+                mbar_arrive_expect_tx(&full_r[rs], kRawBox);
+                tma_2d(raw_u + rs * kRawBox, &maps.a, rb * kRawRow, m0, &full_r[rs]);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 0) {
+        // ---------------- activations by TMA ----------------
+        if (lane == 0) {
+            pdl_wait_prior();
+            for (int ks = 0; ks < a.ksteps; ++ks) {
+                const int s = ks % a.stages;
+                if (ks >= a.stages && !mbar_wait(&empty[s], ((ks / a.stages) - 1) & 1, a.err, kErrBulkTimeout)) break;
+                const uint32_t st = base + s * stage_bytes;
+                mbar_arrive_expect_tx(&full_x[s], 2 * b_bytes);
+                tma_2d(st + 2 * a_bytes, &maps.b0, ks * kStepBytes, n0, &full_x[s]);
+                tma_2d(st + 2 * a_bytes + b_bytes, &maps.b1, ks * kStepBytes, n0, &full_x[s]);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            const uint32_t idesc = instr_desc(1, 0, 0, kTileM, NB);
+            bool ok = true;
+            for (int c = 0; c < nchunks && ok; ++c) {
+                const int slot = c & 1;
+                if (c >= 2 && !mbar_wait(&tfree[slot], ((c >> 1) - 1) & 1, a.err, kErrMmaTimeout)) break;
+                tc_fence_after();
+                const uint32_t d = taddr + slot * NB;
+                const int ks_end = min(a.ksteps, (c + 1) * kChunkSteps);
+                for (int ks = c * kChunkSteps; ks < ks_end; ++ks) {
+                    const int s = ks % a.stages;
+                    const uint32_t par = (ks / a.stages) & 1;
+                    if (!mbar_wait(&full_x[s], par, a.err, kErrBulkTimeout) ||
+                        !mbar_wait(&full_w[s], par, a.err, kErrBulkTimeout)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t st = base + s * stage_bytes;
+                    const uint64_t dh = sw128_desc(st), dl = sw128_desc(st + a_bytes);
+                    const uint64_t xh = sw128_desc(st + 2 * a_bytes), xl = sw128_desc(st + 2 * a_bytes + b_bytes);
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        mma_f16(d, dh + 2 * kk, xh + 2 * kk, idesc, (ks != c * kChunkSteps) || kk != 0);
+                        mma_f16(d, dh + 2 * kk, xl + 2 * kk, idesc, 1);
+                        mma_f16(d, dl + 2 * kk, xh + 2 * kk, idesc, 1);
+                    }
+                    mma_commit(&empty[s]);
+                }
+                mma_commit(&tfull[slot]);
+            }
+        }
+        __syncwarp();
+    } else if (warp < 6) {
+        // ---------------- epilogue: chunk sums in f32 registers ----------------
+        const int quarter = warp & 3;
+        const int row = m0 + quarter * 32 + lane;
+        const uint32_t lane_addr = taddr + (static_cast<uint32_t>(quarter * 32) << 16);
+        float sum[NB];
+#pragma unroll
+        for (int i = 0; i < NB; ++i) sum[i] = 0.f;
+        bool ok = true;
+        for (int c = 0; c < nchunks; ++c) {
+            const int slot = c & 1;
+            if (!mbar_wait(&tfull[slot], (c >> 1) & 1, a.err, kErrMmaTimeout)) { ok = false; break; }
+            tc_fence_after();
+#pragma unroll
+            for (int c0 = 0; c0 < NB; c0 += 16) {
+                uint32_t p[16];
+                tmem_ld16(lane_addr + slot * NB + c0, p);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 16; ++i) sum[c0 + i] = __fadd_rn(sum[c0 + i], __uint_as_float(p[i]));
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tfree[slot]);
+        }
+        if (ok && row < a.n) {
+#pragma unroll
+            for (int i = 0; i < NB; ++i) {
+                const int col = n0 + i;
+                if (col < a.batch) a.y[static_cast<long long>(col) * a.y_stride + row] = __fmul_rn(sum[i], a.col_scale[col]);
+            }
+        }
+    } else {
+        // ---------------- dequantisers: one weight row per thread ----------------
+        const int rt = threadIdx.x - 192;  // row in the tile
+        const uint32_t row_off = (rt >> 3) * 1024 + (rt & 7) * 128;  // swizzled tile row
+        const uint32_t sw = rt & 7;
+        bool ok = true;
+        for (int rb = 0; rb < nbox && ok; ++rb) {
+            const int rs = rb % a.raw_slots;
+            if (!mbar_wait(&full_r[rs], (rb / a.raw_slots) & 1, a.err, kErrBulkTimeout)) break;
+            uint32_t w[36];  // this row's four K steps: per step two blocks (2-byte scale + 16 nibble bytes)
+            const uint32_t rp = raw_u + rs * kRawBox + rt * kRawRow;
+#pragma unroll
+            for (int c = 0; c < 9; ++c)
+                asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                             : "=r"(w[4 * c]), "=r"(w[4 * c + 1]), "=r"(w[4 * c + 2]), "=r"(w[4 * c + 3])
+                             : "r"(rp + 16 * c));
+            mbar_arrive(&empty_r[rs]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int ks = 4 * rb + j;
+                const int s = ks % a.stages;
+                if (ks >= a.stages && !mbar_wait(&empty[s], ((ks / a.stages) - 1) & 1, a.err, kErrBulkTimeout)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t th = base + s * stage_bytes + row_off, tl = th + a_bytes;
+                const uint32_t *v = w + 9 * j;
+                // block 0: scale in bytes 0-1, nibbles in bytes 2-17; block 1: scale 18-19, nibbles 20-35
+                const uint32_t d0 = __byte_perm(v[0], v[0], 0x1010), d1 = __byte_perm(v[4], v[4], 0x3232);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    uint4 h, l;
+                    q4_chunk(__byte_perm(v[q], v[q + 1], 0x5432), d0, h, l);
+                    sts128(th + ((q ^ sw) << 4), h);
+                    sts128(tl + ((q ^ sw) << 4), l);
+                    q4_chunk(v[5 + q], d1, h, l);
+                    sts128(th + (((4 + q) ^ sw) << 4), h);
+                    sts128(tl + (((4 + q) ^ sw) << 4), l);
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> MMA reads
+                mbar_arrive(&full_w[s]);
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(taddr, a.tmem_cols);
     }
 }
 
 // Activation rows for the f16 kernel: x[b, :] = 2^e[b] * (hi + lo), e chosen so that the
 // row's largest magnitude lies in [2^14, 2^15) (f16 hi/lo keep ~22 bits for
 // values down to ~2^-28 of it).  One CTA per row.
+// (permute: K positions in the q4_pos order of each 32-element block).
 __global__ void __launch_bounds__(256) split_rows_kernel(const float *x, int k, int x_stride, __half *hi, __half *lo,
-                                                         float *scale) {
+                                                         float *scale, int permute) {
     __shared__ uint32_t red[8];
     const float *src = x + static_cast<long long>(blockIdx.x) * x_stride;
     uint32_t m = 0;
@@ -440,8 +648,9 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const float *x, int k, 
         const float v = __fmul_rn(src[j], s);
         const __half hv = __float2half_rn(v);
         const float hf = __half2float(hv);
-        h[j] = hv;
-        l[j] = (__float_as_uint(hf) & 0x7fffffffu) < 0x7f800000u ? __float2half_rn(__fsub_rn(v, hf)) : __ushort_as_half(0);
+        const int p = permute ? (j & ~31) + q4_pos(j & 31) : j;
+        h[p] = hv;
+        l[p] = (__float_as_uint(hf) & 0x7fffffffu) < 0x7f800000u ? __float2half_rn(__fsub_rn(v, hf)) : __ushort_as_half(0);
     }
     if (threadIdx.x == 0) scale[blockIdx.x] = __uint_as_float(static_cast<uint32_t>(e + 127) << 23);
 }
@@ -476,13 +685,27 @@ bool encode_kmajor(CUtensorMap &m, const void *ptr, long long row_bytes, int row
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// q4_0 weights [rows][row_bytes], boxes of 128 rows x 144 bytes, no swizzle.
+bool encode_raw_boxes(CUtensorMap &m, const void *ptr, long long row_bytes, int rows) {
+    auto fn = tc_encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(kRawRow), static_cast<cuuint32_t>(kTileM)};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace
 
 bool gemm_tc_supported(int wt, int k, int n, int batch) {
     (void)n;
     if (k % 16) return false;
     if (wt == 3 || wt == 1) return batch >= kTcMinBatch;
-    return wt == 2 && batch >= kTcMinBatchQ4;
+    // q4: raw boxes of 4 K steps (256 elements) and 16-byte multiple row strides
+    return wt == 2 && batch >= kTcMinBatchQ4 && k % 256 == 0;
 }
 
 namespace {
@@ -490,20 +713,22 @@ size_t align256(size_t b) { return (b + 255) & ~size_t(255); }
 }  // namespace
 
 size_t gemm_tc_scratch_bytes(int wt, int k, int n, int batch) {
+    (void)n;
     if (wt != 1 && wt != 2) return 0;
-    size_t bytes = 2 * align256(static_cast<size_t>(batch) * k * 2) + align256(static_cast<size_t>(batch) * 4);
-    if (wt == 2) bytes += 2 * align256(static_cast<size_t>(n) * k * 2);  // expanded weights, hi and lo
-    return bytes;
+    return 2 * align256(static_cast<size_t>(batch) * k * 2) + align256(static_cast<size_t>(batch) * 4);
 }
 
 cudaError_t launch_gemm_tc(const GemvRequest &r, const DeviceInfo &dev, cudaStream_t stream) {
     if (!gemm_tc_supported(r.wt, r.k, r.n, r.batch)) return cudaErrorNotSupported;
     const bool i8 = r.wt == 3, q4 = r.wt == 2;
     if (reinterpret_cast<uintptr_t>(r.w) & 15) return cudaErrorNotSupported;
+    if (q4 && r.k % 256) return cudaErrorNotSupported;  // whole raw boxes, 16-byte multiple rows
     if (i8 && ((reinterpret_cast<uintptr_t>(r.q) & 15) || (r.q_comp & 15) || r.q_stride != r.k))
         return cudaErrorNotSupported;
     if (!i8 && (!r.split || r.split_bytes < gemm_tc_scratch_bytes(r.wt, r.k, r.n, r.batch))) return cudaErrorNotSupported;
     TcArgs a{};
+    a.w = static_cast<const uint8_t *>(r.w);
+    a.row_bytes = static_cast<long long>(r.k / 32) * 18;
     a.y = r.y;
     a.row_scale = r.row_scale;
     a.act_max = r.act_max;
@@ -512,59 +737,54 @@ cudaError_t launch_gemm_tc(const GemvRequest &r, const DeviceInfo &dev, cudaStre
     a.n = r.n;
     a.batch = r.batch;
     a.y_stride = r.y_stride;
-    const int cap = i8 ? 256 : 128;  // the f16 epilogue keeps NB sums per thread in registers
+    const int cap = i8 ? 256 : 128;  // the f16/q4 epilogue keeps NB sums per thread in registers
     a.nb = r.batch >= cap ? cap : (r.batch + 15) / 16 * 16;
     if (!i8) a.nb = a.nb <= 16 ? 16 : a.nb <= 32 ? 32 : a.nb <= 64 ? 64 : 128;
-    const long long row_bytes = i8 ? r.k : 2ll * r.k;
+    const long long row_bytes = i8 ? r.k : 2ll * r.k;  // bytes per row of the MMA operands
     a.ksteps = static_cast<int>((row_bytes + kStepBytes - 1) / kStepBytes);
     uint32_t cols = 32;
     while (cols < static_cast<uint32_t>(2 * a.nb)) cols <<= 1;  // two accumulators or two slots
     a.tmem_cols = cols;
     const size_t stage = static_cast<size_t>(kTileM) * kStepBytes * (q4 ? 2 : 1) + 2 * static_cast<size_t>(a.nb) * kStepBytes;
-    const size_t budget = static_cast<size_t>(dev.smem_optin) - 1024 - 256;
-    int stages = static_cast<int>(budget / stage);
+    // q4: four raw slots while that leaves three operand stages, else three
+    int raw_slots = q4 ? 4 : 0, stages = 0;
+    for (;;) {
+        const size_t fixed = q4 ? kBarBytesQ4 + static_cast<size_t>(raw_slots) * kRawBox : 256;
+        stages = static_cast<int>((static_cast<size_t>(dev.smem_optin) - 1024 - fixed) / stage);
+        if (!q4 || stages >= 3 || raw_slots == 3) break;
+        --raw_slots;
+    }
     if (stages > 6) stages = 6;
     if (stages < 2) return cudaErrorNotSupported;
     a.stages = stages;
-    const size_t smem = 1024 + stages * stage + 256;
+    a.raw_slots = raw_slots;
+    const size_t smem = 1024 + stages * stage + (q4 ? kBarBytesQ4 + static_cast<size_t>(raw_slots) * kRawBox : 256);
     TcMaps maps;
-    const void *w0 = r.w, *w1 = r.w, *b0 = r.q, *b1 = r.q ? r.q + r.q_comp : nullptr;
+    const void *b0 = r.q, *b1 = r.q ? r.q + r.q_comp : nullptr;
     if (!i8) {
-        // split the activation rows into f16 hi/lo (scratch: hi | lo | scales | expanded weights)
+        // split the activation rows into f16 hi/lo (scratch: hi | lo | scales)
         const size_t part = align256(static_cast<size_t>(r.batch) * r.k * 2);
-        char *base = static_cast<char *>(r.split);
-        __half *hi = reinterpret_cast<__half *>(base), *lo = reinterpret_cast<__half *>(base + part);
-        float *sc = reinterpret_cast<float *>(base + 2 * part);
-        split_rows_kernel<<<r.batch, 256, 0, stream>>>(r.x, r.k, r.x_stride, hi, lo, sc);
+        char *sbase = static_cast<char *>(r.split);
+        __half *hi = reinterpret_cast<__half *>(sbase), *lo = reinterpret_cast<__half *>(sbase + part);
+        float *sc = reinterpret_cast<float *>(sbase + 2 * part);
+        split_rows_kernel<<<r.batch, 256, 0, stream>>>(r.x, r.k, r.x_stride, hi, lo, sc, q4 ? 1 : 0);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
         b0 = hi;
         b1 = lo;
         a.col_scale = sc;
-        if (q4) {
-            char *wbase = base + 2 * part + align256(static_cast<size_t>(r.batch) * 4);
-            const size_t wpart = align256(static_cast<size_t>(r.n) * r.k * 2);
-            __half *whi = reinterpret_cast<__half *>(wbase), *wlo = reinterpret_cast<__half *>(wbase + wpart);
-            const long long blocks = static_cast<long long>(r.n) * (r.k / 32);
-            dequant_q4_split_kernel<<<static_cast<unsigned>((blocks + 255) / 256), 256, 0, stream>>>(
-                static_cast<const uint8_t *>(r.w), static_cast<long long>(r.k / 32) * 18, r.k, r.n, whi, wlo);
-            e = cudaGetLastError();
-            if (e != cudaSuccess) return e;
-            w0 = whi;
-            w1 = wlo;
-        }
     }
-    if (!encode_kmajor(maps.a, w0, row_bytes, r.n, kTileM) || !encode_kmajor(maps.a1, w1, row_bytes, r.n, kTileM) ||
+    if ((q4 ? !encode_raw_boxes(maps.a, r.w, a.row_bytes, r.n) : !encode_kmajor(maps.a, r.w, row_bytes, r.n, kTileM)) ||
         !encode_kmajor(maps.b0, b0, row_bytes, r.batch, a.nb) || !encode_kmajor(maps.b1, b1, row_bytes, r.batch, a.nb))
         return cudaErrorNotSupported;
     void (*kern)(TcMaps, TcArgs) = gemm_i8_kernel;
     int ki = 0;
     if (!i8) {
         const int which = a.nb == 16 ? 0 : a.nb == 32 ? 1 : a.nb == 64 ? 2 : 3;
-        static void (*const f16k[4])(TcMaps, TcArgs) = {gemm_f16_kernel<16, false>, gemm_f16_kernel<32, false>,
-                                                          gemm_f16_kernel<64, false>, gemm_f16_kernel<128, false>};
-        static void (*const q4k[4])(TcMaps, TcArgs) = {gemm_f16_kernel<16, true>, gemm_f16_kernel<32, true>,
-                                                         gemm_f16_kernel<64, true>, gemm_f16_kernel<128, true>};
+        static void (*const f16k[4])(TcMaps, TcArgs) = {gemm_f16_kernel<16>, gemm_f16_kernel<32>, gemm_f16_kernel<64>,
+                                                          gemm_f16_kernel<128>};
+        static void (*const q4k[4])(TcMaps, TcArgs) = {gemm_q4_kernel<16>, gemm_q4_kernel<32>, gemm_q4_kernel<64>,
+                                                         gemm_q4_kernel<128>};
         kern = q4 ? q4k[which] : f16k[which];
         ki = 1 + which + (q4 ? 4 : 0);
     }
@@ -578,7 +798,7 @@ cudaError_t launch_gemm_tc(const GemvRequest &r, const DeviceInfo &dev, cudaStre
     }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((r.n + kTileM - 1) / kTileM, (r.batch + a.nb - 1) / a.nb);
-    cfg.blockDim = dim3(kThreadsTc);
+    cfg.blockDim = dim3(q4 ? kThreadsQ4 : kThreadsTc);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];

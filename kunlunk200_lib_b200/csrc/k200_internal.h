@@ -50,8 +50,8 @@ size_t q4_mma_scratch_bytes(int k, int n, int batch, const DeviceInfo &dev);
 // q4_0 weights with f32 activations (which need gemm_tc_scratch_bytes of
 // scratch in GemvRequest::split).
 constexpr int kTcMinBatch = 4;
-constexpr int kTcMinBatchQ4 = 8;   // q4_0: the weights are expanded to f16 hi/lo first
-bool gemm_tc_supported(int wt, int k, int n, int batch);
+constexpr int kTcMinBatchQ4 = 4;
+bool gemm_tc_supported(int wt, int k, int n, int batch);  // (q4_0 also needs k % 64 == 0)
 size_t gemm_tc_scratch_bytes(int wt, int k, int n, int batch);
 cudaError_t launch_gemm_tc(const GemvRequest &r, const DeviceInfo &dev, cudaStream_t stream);
 cudaError_t launch_q4_mma_gemv(const GemvRequest &r, const DeviceInfo &dev, cudaStream_t stream);

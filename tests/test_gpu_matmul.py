@@ -103,11 +103,13 @@ def test_q4_0_matches_fp64_gold(K, O, gpu, k, n, batch):
     _check_float(y, gold)
 
 
-@pytest.mark.parametrize("k,n,batch", [(4096, 1024, 32), (4096, 512, 128), (1056, 300, 300)])
+@pytest.mark.parametrize("k,n,batch", [(4096, 1024, 32), (4096, 512, 128), (1280, 300, 300), (4096, 256, 4),
+                                       (4096, 1000, 16), (2048, 129, 520), (1088, 300, 300), (1056, 300, 300)])
 def test_q4_0_batched_tensor_cores(K, O, gpu, k, n, batch):
-    """Config 2 class (batched q4_0 on the tensor cores after the f16 hi/lo
-    weight expansion), held to the reference's q4_0 bar (library-bench tol
-    1e-3) and an NMSE far below it."""
+    """Config 2 class (batched q4_0 on the tensor cores, dequantised in the
+    kernel to exact f16 hi/lo halves), held to the reference's q4_0 bar
+    (library-bench tol 1e-3) and an NMSE far below it.  K = 1088 and 1056
+    (not multiples of 256) take the streaming kernels."""
     q4, x = _q4_case(O, k, n, batch)
     y = _device_matmul(K, K.Q4_0, q4, x, k, n, batch)
     gold = O.matmul_gold(q4, O.WT_Q4_0, x, k, n, batch)
