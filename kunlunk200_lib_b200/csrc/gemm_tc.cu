@@ -37,13 +37,18 @@
 //    global memory and write W' = d*(q-8) into shared memory as exact f16
 //    hi + lo halves (hi = f16(d*(q-8)), lo = fma(d, q-8, -hi): the residual
 //    has at most 3 significant bits) in the swizzled layout the MMA reads.
-//    The raw blocks arrive by TMA in boxes of 128 rows x 144 bytes (four
-//    K steps) through a ring of 3-4 slots filled by a dedicated producer
-//    warp; each dequantiser reads its row's 144 bytes with nine
-//    conflict-free 16-byte shared loads.  (Per-thread global loads of the
-//    36-byte row pieces touch 32 sectors per instruction and saturate L1.)
-//    Three products per K step: hi*x_hi + hi*x_lo + lo*x_hi (lo*x_lo is
-//    below 2^-21 of the term).  Each 16-byte chunk holds one decoded nibble
+//    The raw blocks arrive by TMA in boxes of 128 rows x 288 bytes (eight
+//    K steps) through a ring of 2-3 slots filled by a dedicated producer
+//    warp; each dequantiser reads its row's bytes with 16-byte shared loads.
+//    (Per-thread global loads of the 36-byte row pieces touch 32 sectors per
+//    instruction and saturate L1; a TMA box costs the copy engine about the
+//    same per row whatever the row's width, so rows are made wide.)
+//    Three products per K slice: hi*x_hi + hi*x_lo + lo*x_hi (lo*x_lo is
+//    below 2^-21 of the term), issued as two MMAs: W hi against the x hi and
+//    x lo tiles as one 2NB-row operand, and W lo against x hi.  (An MMA of
+//    M = 128, K = 16 occupies the tensor pipe for at least ~45 cycles
+//    whatever N is below 128, so fewer, wider MMAs are what small batches
+//    need.)  Each 16-byte chunk holds one decoded nibble
 //    word in the order the decode produces, and the activations are split
 //    into the same permuted K order (q4_pos below), so the sums are those of
 //    the natural order.
@@ -385,8 +390,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1) gemm_f16_kernel(const __grid_co
 
 // ---- q4_0 with in-kernel dequantisation -------------------------------------
 constexpr int kThreadsQ4 = 352;  // x TMA, MMA, 4 x epilogue, 4 x dequantiser, weight TMA
-constexpr int kRawRow = 144;     // bytes of one weight row per raw box: 4 K steps of 2 blocks
-constexpr int kRawBox = kTileM * kRawRow;  // 18 KB
+constexpr int kRawSteps = 8;                // K steps (pairs of blocks) per raw box
+constexpr int kRawRow = 36 * kRawSteps;     // 288 bytes of one weight row per raw box
+constexpr int kRawBox = kTileM * kRawRow;   // 36 KB
 constexpr int kBarBytesQ4 = 1024;          // mbarriers and the TMEM slot
 
 // Position of element e (0..31) of a block inside the block's 32 K positions
@@ -448,7 +454,7 @@ __global__ void __launch_bounds__(kThreadsQ4, 1) gemm_q4_kernel(const __grid_con
     uint64_t *empty_r = full_r + a.raw_slots;  // raw box read by all 128 dequantisers
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(empty_r + a.raw_slots);
     const uint32_t raw_u = base + a.stages * stage_bytes + kBarBytesQ4;  // raw ring [slot][row][144 B]
-    const int nbox = a.ksteps / 4;
+    const int nbox = (a.ksteps + kRawSteps - 1) / kRawSteps;  // the last box may run past the row (zero fill)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.x * kTileM, n0 = blockIdx.y * NB;
@@ -486,7 +492,7 @@ __global__ void __launch_bounds__(kThreadsQ4, 1) gemm_q4_kernel(const __grid_con
                     !mbar_wait(&empty_r[rs], ((rb / a.raw_slots) - 1) & 1, a.err, kErrBulkTimeout))
                     break;
                 mbar_arrive_expect_tx(&full_r[rs], kRawBox);
-                tma_2d(raw_u + rs * kRawBox, &maps.a, rb * kRawRow, m0, &full_r[rs]);
+                tma_2d(raw_u + rs * kRawBox, &maps.a, rb * (kRawRow / 4), m0, &full_r[rs]);
             }
         }
         __syncwarp();
@@ -507,13 +513,14 @@ __global__ void __launch_bounds__(kThreadsQ4, 1) gemm_q4_kernel(const __grid_con
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            const uint32_t idesc = instr_desc(1, 0, 0, kTileM, NB);
+            // x hi and x lo are adjacent NB-row tiles: one 2NB-row operand
+            const uint32_t idesc2 = instr_desc(1, 0, 0, kTileM, 2 * NB), idesc1 = instr_desc(1, 0, 0, kTileM, NB);
             bool ok = true;
             for (int c = 0; c < nchunks && ok; ++c) {
                 const int slot = c & 1;
                 if (c >= 2 && !mbar_wait(&tfree[slot], ((c >> 1) - 1) & 1, a.err, kErrMmaTimeout)) break;
                 tc_fence_after();
-                const uint32_t d = taddr + slot * NB;
+                const uint32_t d = taddr + slot * 2 * NB;  // [W*x hi | W hi*x lo]
                 const int ks_end = min(a.ksteps, (c + 1) * kChunkSteps);
                 for (int ks = c * kChunkSteps; ks < ks_end; ++ks) {
                     const int s = ks % a.stages;
@@ -523,12 +530,11 @@ __global__ void __launch_bounds__(kThreadsQ4, 1) gemm_q4_kernel(const __grid_con
                     tc_fence_after();
                     const uint32_t st = base + s * stage_bytes;
                     const uint64_t dh = sw128_desc(st), dl = sw128_desc(st + a_bytes);
-                    const uint64_t xh = sw128_desc(st + 2 * a_bytes), xl = sw128_desc(st + 2 * a_bytes + b_bytes);
+                    const uint64_t xh = sw128_desc(st + 2 * a_bytes);
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
-                        mma_f16(d, dh + 2 * kk, xh + 2 * kk, idesc, (ks != c * kChunkSteps) || kk != 0);
-                        mma_f16(d, dh + 2 * kk, xl + 2 * kk, idesc, 1);
-                        mma_f16(d, dl + 2 * kk, xh + 2 * kk, idesc, 1);
+                        mma_f16(d, dh + 2 * kk, xh + 2 * kk, idesc2, (ks != c * kChunkSteps) || kk != 0);
+                        mma_f16(d, dl + 2 * kk, xh + 2 * kk, idesc1, 1);
                     }
                     mma_commit(&empty[s]);
                 }
@@ -550,12 +556,12 @@ __global__ void __launch_bounds__(kThreadsQ4, 1) gemm_q4_kernel(const __grid_con
             if (!mbar_wait(&tfull[slot], (c >> 1) & 1, a.err, kErrMmaTimeout)) { ok = false; break; }
             tc_fence_after();
 #pragma unroll
-            for (int c0 = 0; c0 < NB; c0 += 16) {
+            for (int c0 = 0; c0 < 2 * NB; c0 += 16) {
                 uint32_t p[16];
-                tmem_ld16(lane_addr + slot * NB + c0, p);
+                tmem_ld16(lane_addr + slot * 2 * NB + c0, p);
                 tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < 16; ++i) sum[c0 + i] = __fadd_rn(sum[c0 + i], __uint_as_float(p[i]));
+                for (int i = 0; i < 16; ++i) sum[(c0 % NB) + i] = __fadd_rn(sum[(c0 % NB) + i], __uint_as_float(p[i]));
             }
             tc_fence_before();
             __syncwarp();
@@ -577,38 +583,46 @@ __global__ void __launch_bounds__(kThreadsQ4, 1) gemm_q4_kernel(const __grid_con
         for (int rb = 0; rb < nbox && ok; ++rb) {
             const int rs = rb % a.raw_slots;
             if (!mbar_wait(&full_r[rs], (rb / a.raw_slots) & 1, a.err, kErrBulkTimeout)) break;
-            uint32_t w[36];  // this row's four K steps: per step two blocks (2-byte scale + 16 nibble bytes)
-            const uint32_t rp = raw_u + rs * kRawBox + rt * kRawRow;
 #pragma unroll
-            for (int c = 0; c < 9; ++c)
-                asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                             : "=r"(w[4 * c]), "=r"(w[4 * c + 1]), "=r"(w[4 * c + 2]), "=r"(w[4 * c + 3])
-                             : "r"(rp + 16 * c));
-            mbar_arrive(&empty_r[rs]);
+            for (int half = 0; half < kRawSteps / 4 && ok; ++half) {
+                uint32_t w[36];  // four K steps of this row: per step two blocks (2-byte scale + 16 nibble bytes)
+                const uint32_t rp = raw_u + rs * kRawBox + rt * kRawRow + half * 144;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int ks = 4 * rb + j;
-                const int s = ks % a.stages;
-                if (ks >= a.stages && !mbar_wait(&empty[s], ((ks / a.stages) - 1) & 1, a.err, kErrBulkTimeout)) {
-                    ok = false;
-                    break;
+                for (int c = 0; c < 9; ++c)
+                    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                                 : "=r"(w[4 * c]), "=r"(w[4 * c + 1]), "=r"(w[4 * c + 2]), "=r"(w[4 * c + 3])
+                                 : "r"(rp + 16 * c));
+                if (half == kRawSteps / 4 - 1) {
+                    // order these generic reads before the copy engine's next write into the slot
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    mbar_arrive(&empty_r[rs]);
                 }
-                const uint32_t th = base + s * stage_bytes + row_off, tl = th + a_bytes;
-                const uint32_t *v = w + 9 * j;
-                // block 0: scale in bytes 0-1, nibbles in bytes 2-17; block 1: scale 18-19, nibbles 20-35
-                const uint32_t d0 = __byte_perm(v[0], v[0], 0x1010), d1 = __byte_perm(v[4], v[4], 0x3232);
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    uint4 h, l;
-                    q4_chunk(__byte_perm(v[q], v[q + 1], 0x5432), d0, h, l);
-                    sts128(th + ((q ^ sw) << 4), h);
-                    sts128(tl + ((q ^ sw) << 4), l);
-                    q4_chunk(v[5 + q], d1, h, l);
-                    sts128(th + (((4 + q) ^ sw) << 4), h);
-                    sts128(tl + (((4 + q) ^ sw) << 4), l);
+                for (int j = 0; j < 4; ++j) {
+                    const int ks = rb * kRawSteps + half * 4 + j;
+                    if (ks >= a.ksteps) break;
+                    const int s = ks % a.stages;
+                    if (ks >= a.stages && !mbar_wait(&empty[s], ((ks / a.stages) - 1) & 1, a.err, kErrBulkTimeout)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t th = base + s * stage_bytes + row_off, tl = th + a_bytes;
+                    const uint32_t *v = w + 9 * j;
+                    // block 0: scale in bytes 0-1, nibbles in bytes 2-17; block 1: scale 18-19, nibbles 20-35
+                    const uint32_t d0 = __byte_perm(v[0], v[0], 0x1010), d1 = __byte_perm(v[4], v[4], 0x3232);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        uint4 h, l;
+                        q4_chunk(__byte_perm(v[q], v[q + 1], 0x5432), d0, h, l);
+                        sts128(th + ((q ^ sw) << 4), h);
+                        sts128(tl + ((q ^ sw) << 4), l);
+                        q4_chunk(v[5 + q], d1, h, l);
+                        sts128(th + (((4 + q) ^ sw) << 4), h);
+                        sts128(tl + (((4 + q) ^ sw) << 4), l);
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> MMA reads
+                    mbar_arrive(&full_w[s]);
                 }
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> MMA reads
-                mbar_arrive(&full_w[s]);
             }
         }
     }
@@ -685,15 +699,16 @@ bool encode_kmajor(CUtensorMap &m, const void *ptr, long long row_bytes, int row
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// q4_0 weights [rows][row_bytes], boxes of 128 rows x 144 bytes, no swizzle.
+// q4_0 weights [rows][row_bytes] as 4-byte elements, boxes of 128 rows x
+// kRawRow bytes, no swizzle (a box past the row end reads zeros).
 bool encode_raw_boxes(CUtensorMap &m, const void *ptr, long long row_bytes, int rows) {
     auto fn = tc_encode_fn();
     if (!fn) return false;
-    cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(rows)};
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes / 4), static_cast<cuuint64_t>(rows)};
     cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
-    cuuint32_t box[2] = {static_cast<cuuint32_t>(kRawRow), static_cast<cuuint32_t>(kTileM)};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(kRawRow / 4), static_cast<cuuint32_t>(kTileM)};
     cuuint32_t estr[2] = {1, 1};
-    return fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+    return fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void *>(ptr), dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -704,7 +719,7 @@ bool gemm_tc_supported(int wt, int k, int n, int batch) {
     (void)n;
     if (k % 16) return false;
     if (wt == 3 || wt == 1) return batch >= kTcMinBatch;
-    // q4: raw boxes of 4 K steps (256 elements) and 16-byte multiple row strides
+    // q4: 16-byte multiple row strides (36 * k / 64 bytes)
     return wt == 2 && batch >= kTcMinBatchQ4 && k % 256 == 0;
 }
 
@@ -722,7 +737,7 @@ cudaError_t launch_gemm_tc(const GemvRequest &r, const DeviceInfo &dev, cudaStre
     if (!gemm_tc_supported(r.wt, r.k, r.n, r.batch)) return cudaErrorNotSupported;
     const bool i8 = r.wt == 3, q4 = r.wt == 2;
     if (reinterpret_cast<uintptr_t>(r.w) & 15) return cudaErrorNotSupported;
-    if (q4 && r.k % 256) return cudaErrorNotSupported;  // whole raw boxes, 16-byte multiple rows
+    if (q4 && r.k % 256) return cudaErrorNotSupported;  // 16-byte multiple rows
     if (i8 && ((reinterpret_cast<uintptr_t>(r.q) & 15) || (r.q_comp & 15) || r.q_stride != r.k))
         return cudaErrorNotSupported;
     if (!i8 && (!r.split || r.split_bytes < gemm_tc_scratch_bytes(r.wt, r.k, r.n, r.batch))) return cudaErrorNotSupported;
@@ -743,15 +758,16 @@ cudaError_t launch_gemm_tc(const GemvRequest &r, const DeviceInfo &dev, cudaStre
     const long long row_bytes = i8 ? r.k : 2ll * r.k;  // bytes per row of the MMA operands
     a.ksteps = static_cast<int>((row_bytes + kStepBytes - 1) / kStepBytes);
     uint32_t cols = 32;
-    while (cols < static_cast<uint32_t>(2 * a.nb)) cols <<= 1;  // two accumulators or two slots
+    // i8: two accumulators; f16: two chunk slots; q4: two chunk slots of 2 x nb columns
+    while (cols < static_cast<uint32_t>((q4 ? 4 : 2) * a.nb)) cols <<= 1;
     a.tmem_cols = cols;
     const size_t stage = static_cast<size_t>(kTileM) * kStepBytes * (q4 ? 2 : 1) + 2 * static_cast<size_t>(a.nb) * kStepBytes;
-    // q4: four raw slots while that leaves three operand stages, else three
-    int raw_slots = q4 ? 4 : 0, stages = 0;
+    // q4: three raw slots while that leaves three operand stages, else two
+    int raw_slots = q4 ? 3 : 0, stages = 0;
     for (;;) {
         const size_t fixed = q4 ? kBarBytesQ4 + static_cast<size_t>(raw_slots) * kRawBox : 256;
         stages = static_cast<int>((static_cast<size_t>(dev.smem_optin) - 1024 - fixed) / stage);
-        if (!q4 || stages >= 3 || raw_slots == 3) break;
+        if (!q4 || stages >= 3 || raw_slots == 2) break;
         --raw_slots;
     }
     if (stages > 6) stages = 6;

@@ -524,6 +524,8 @@ __global__ void __maxnreg__((Shape<WT, B>::maxreg)) gemv_stream_kernel(const Gem
                 }
             }
         }
+        // order this thread's reads of the stage before the next TMA write into it
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         if (wps > 1) {
             // all warps of the slot have deposited: sum each row in warp order
             asm volatile("bar.sync %0, %1;" ::"r"(1 + slot), "r"(a.tpr) : "memory");

@@ -587,10 +587,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             acc[2] = fmaf(s2, d1[0] + d1[1], acc[2]);
             acc[3] = fmaf(s3, d1[2] + d1[3], acc[3]);
         }
-        // the last warp to finish a pair of this box releases the stage
+        // the last warp to finish a pair of this box releases the stage; the
+        // proxy fence orders this warp's reads before the next TMA write into it
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
         if (lane == 0) {
+            __threadfence_block();
             if (atomicAdd(&done[s], 1) == width - 1) {
+                __threadfence_block();
                 done[s] = 0;
                 mbar_arrive(&empty[s]);
             }
