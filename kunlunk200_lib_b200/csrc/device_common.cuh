@@ -115,18 +115,8 @@ __device__ __forceinline__ unsigned long long u2_pack(uint32_t lo, uint32_t hi) 
 __device__ __forceinline__ unsigned long long f2_pack(float lo, float hi) {
     return u2_pack(__float_as_uint(lo), __float_as_uint(hi));
 }
-__device__ __forceinline__ float f2_lo(unsigned long long v) {
-    uint32_t lo, hi;
-    asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(v));
-    (void)hi;
-    return __uint_as_float(lo);
-}
-__device__ __forceinline__ float f2_hi(unsigned long long v) {
-    uint32_t lo, hi;
-    asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(v));
-    (void)lo;
-    return __uint_as_float(hi);
-}
+__device__ __forceinline__ float f2_lo(unsigned long long v) { return __uint_as_float(static_cast<uint32_t>(v)); }
+__device__ __forceinline__ float f2_hi(unsigned long long v) { return __uint_as_float(static_cast<uint32_t>(v >> 32)); }
 // lo + hi of a pair
 __device__ __forceinline__ float f2_sum(unsigned long long v) {
     uint32_t lo, hi;

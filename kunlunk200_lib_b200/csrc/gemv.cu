@@ -89,7 +89,6 @@ __device__ __forceinline__ int vec_index(int seg, int lw, int per_thread, int v)
 template <int WT, int B>
 struct Shape {
     static constexpr int xregs = (WT == 0 || WT == 3) ? 32 * B : 64 * B;
-    static constexpr int ilp = xregs <= 64 ? 2 : 1;
     static constexpr int consumers = xregs <= 64 ? 448 : 256;
     static constexpr int threads = consumers + 32;  // + one producer warp
     // registers per thread that still fit one CTA in the 64K register file

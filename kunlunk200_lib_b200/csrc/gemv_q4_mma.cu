@@ -21,11 +21,13 @@
 //    contiguous range of them, so the bytes per CTA are balanced to within
 //    one pair;
 //  * a producer thread streams the CTA's range through a ring of stages with
-//    2-D TMA tensor copies (cp.async.bulk.tensor + mbarriers) of boxes up to
-//    seven pairs wide (32 rows x 1008 bytes), using 5-, 3- and 1-pair boxes
-//    at the ends of a row tile or of the range.  Measured on B200: boxes
-//    with 144-byte rows stream at ~2 TB/s (the copy engine's cost is per
-//    box row), 432-1008-byte rows at 5.3-6.2 TB/s.  Odd widths keep the
+//    2-D TMA tensor copies (cp.async.bulk.tensor + mbarriers) of boxes of
+//    five or three pairs (32 rows x 720 or 432 bytes); each row tile's part
+//    of the range is cut into 5s and 3s, with 1-pair boxes only for
+//    segments of 1, 2, 4 or 7 pairs.  Measured on B200: boxes with 144-byte
+//    rows stream at ~2 TB/s, 432-1008-byte rows at 5.3-6.7 TB/s; the ring
+//    holds as many 23 KB stages as shared memory allows (6-8), since the
+//    bytes in flight per SM set the streaming rate.  Odd widths keep the
 //    shared-memory row pitch (36*w words) conflict-free for the lane pattern
 //    below;
 //  * consumer warp w processes pairs w, w + 16, ... of the range.  A stage
@@ -66,10 +68,9 @@ namespace {
 constexpr int kTileRows = 32;
 constexpr int kPairBytes = 144;                        // two groups of four blocks
 constexpr int kPairWords = kPairBytes / 4;
-constexpr int kGroupBytes = 72;
-constexpr int kMaxBoxPairs = 7;                        // widest box: 32 rows x 1008 bytes
-constexpr int kStageBytes = kTileRows * kPairBytes * kMaxBoxPairs;  // 32256
-constexpr int kStages = 4;                             // ring stages: 4 x 32 KB in flight streams at ~6 TB/s
+constexpr int kMaxBoxPairs = 5;                        // widest box: 32 rows x 720 bytes
+constexpr int kStageBytes = kTileRows * kPairBytes * kMaxBoxPairs;  // 23040
+constexpr int kMinStages = 4, kMaxStages = 8;         // ring stages: as many as shared memory holds
 constexpr int kRecBytes = 544;                         // fragment record of one group
 constexpr int kZeroOff = 512, kScaleOff = 528;
 constexpr int kWarps = 16;                             // consumer warps
@@ -80,33 +81,50 @@ struct Q4MmaArgs {
     float *y;
     unsigned long long *slot;  // [grid][32] tagged partial sums of row tiles shared with other CTAs
     int *err;
-    long long units;    // row tiles * pairs per row
+    uint32_t units;     // row tiles * pairs per row (units * (grid + 1) < 2^32: 32-bit index math)
     int k, n, tiles, ppr, grid, prefetch;
     int max_tiles;      // row tiles any CTA touches (partial-sum slots in shared memory)
+    int stages;         // ring stages (kMinStages..kMaxStages)
 };
 
 // Tensor maps over the weight rows viewed as 32-bit words [n][row_bytes/4],
-// with boxes of 32 rows x 7, 5, 3 and 1 pairs.
+// with boxes of 32 rows x 5, 3 and 1 pairs.
 struct Q4MmaMaps {
-    CUtensorMap box[4];
+    CUtensorMap box[3];
 };
 __host__ __device__ constexpr int map_of_width(int w) { return (kMaxBoxPairs - w) / 2; }
 
-// The CTA's pairs [u, end) covered by boxes: each row tile's part of the
-// range is cut into 7-pair boxes and a remainder r < 7 (r odd: one r-pair
-// box; r even: an (r-1)-pair and a 1-pair box).  The producer walks this
-// sequence; consumers locate a pair in it with box_of().
+// A segment of L pairs (a row tile's part of a CTA's range) is covered by
+// f5 five-pair boxes, then n3 three-pair boxes, then n1 one-pair boxes, with
+// 5*f5 + 3*n3 + n1 = L and n1 > 0 only for L = 1, 2, 4, 7.  The
+// decomposition of the remaining L - w after a first box of width w is the
+// rest of the decomposition of L, so a walk can pick each box from what is
+// left of the segment.
+struct Decomp {
+    int f5, n3, n1;
+};
+__host__ __device__ inline Decomp decomp(int L) {
+    const int f = L / 5, r = L - 5 * f;
+    if (r == 0) return {f, 0, 0};
+    if (r == 3) return {f, 1, 0};
+    if (r == 1) return f >= 1 ? Decomp{f - 1, 2, 0} : Decomp{0, 0, 1};
+    if (r == 4) return f >= 1 ? Decomp{f - 1, 3, 0} : Decomp{0, 1, 1};
+    return f >= 2 ? Decomp{f - 2, 4, 0} : f == 1 ? Decomp{0, 2, 1} : Decomp{0, 0, 2};  // r == 2
+}
+
+// The CTA's pairs [u, end) covered by boxes, segment by segment.  The
+// producer walks this sequence; consumers locate a pair in it with box_of().
 struct BoxWalk {
-    long long u, end;
+    int u, end;
     int tile, pair, width, ppr;
-    __device__ BoxWalk(long long begin, long long end_, int ppr_) : u(begin), end(end_), ppr(ppr_) {
-        tile = static_cast<int>(begin / ppr);
-        pair = static_cast<int>(begin - static_cast<long long>(tile) * ppr);
+    __device__ BoxWalk(int begin, int end_, int ppr_) : u(begin), end(end_), ppr(ppr_) {
+        tile = begin / ppr;
+        pair = begin - tile * ppr;
         fit();
     }
     __device__ void fit() {
-        const long long left = min(static_cast<long long>(ppr - pair), end - u);
-        width = left >= 7 ? 7 : left >= 5 ? 5 : left >= 3 ? 3 : 1;
+        const Decomp d = decomp(min(ppr - pair, end - u));
+        width = d.f5 ? 5 : d.n3 ? 3 : 1;
     }
     __device__ void next() {
         u += width;
@@ -118,8 +136,8 @@ struct BoxWalk {
 
 // Boxes that cover a segment of L pairs.
 __device__ __forceinline__ int boxes_in(int L) {
-    const int f = L / 7, r = L - 7 * f;
-    return f + (r == 0 ? 0 : (r & 1) ? 1 : 2);
+    const Decomp d = decomp(L);
+    return d.f5 + d.n3 + d.n1;
 }
 
 // Position of a pair in the box sequence: segment [s0, s1) of its row tile
@@ -128,17 +146,22 @@ struct BoxPos {
     int box, q, width;  // box index in the CTA's sequence, pair within box, box width
 };
 __device__ __forceinline__ BoxPos box_of(int p, int s0, int s1, int before) {
-    const int o = p - s0, L = s1 - s0;
-    const int f = L / 7, r = L - 7 * f;
+    const int o = p - s0;
+    const Decomp d = decomp(s1 - s0);
     BoxPos b;
-    if (o < 7 * f) {
-        b.box = o / 7;
-        b.q = o - 7 * b.box;
-        b.width = 7;
+    if (o < 5 * d.f5) {
+        b.box = o / 5;
+        b.q = o - 5 * b.box;
+        b.width = 5;
+    } else if (o < 5 * d.f5 + 3 * d.n3) {
+        const int o2 = o - 5 * d.f5, k3 = o2 / 3;
+        b.box = d.f5 + k3;
+        b.q = o2 - 3 * k3;
+        b.width = 3;
     } else {
-        const int o2 = o - 7 * f, w1 = (r & 1) ? r : r - 1;
-        if (o2 < w1) { b.box = f; b.q = o2; b.width = w1; }
-        else { b.box = f + 1; b.q = 0; b.width = 1; }
+        b.box = d.f5 + d.n3 + (o - 5 * d.f5 - 3 * d.n3);
+        b.q = 0;
+        b.width = 1;
     }
     b.box += before;
     return b;
@@ -233,11 +256,6 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
         : "memory");
 }
 
-__device__ __forceinline__ uint32_t lds(uint32_t addr) {
-    uint32_t v;
-    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
-    return v;
-}
 template <int OFF>
 __device__ __forceinline__ uint32_t lds_at(uint32_t addr) {
     uint32_t v;
@@ -260,8 +278,8 @@ __device__ __forceinline__ void consumer_sync() {
 }
 
 // CTA that processes unit u (CTA i owns units [i*U/G, (i+1)*U/G)).
-__device__ __forceinline__ int cta_of(long long u, long long units, int grid) {
-    return static_cast<int>(((u + 1) * grid - 1) / units);
+__device__ __forceinline__ int cta_of(uint32_t u, uint32_t units, int grid) {
+    return static_cast<int>(((u + 1) * static_cast<uint32_t>(grid) - 1) / units);
 }
 
 // One B-fragment slot pair of an activation block is built by the four
@@ -337,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     q4_mma_gemv_kernel(const __grid_constant__ Q4MmaMaps maps, const Q4MmaArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int groups = a.k >> 7;
-    constexpr int S = kStages;
+    const int S = a.stages;
     uint8_t *ring = smem;
     uint8_t *xrec = ring + S * kStageBytes;
     float *part = reinterpret_cast<float *>(xrec + groups * kRecBytes);  // [max_tiles][kWarps][32]
@@ -348,11 +366,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     int *tcnt = done + S;                                               // [max_tiles] warp arrivals
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const long long u0 = static_cast<long long>(blockIdx.x) * a.units / a.grid;
-    const long long u1 = static_cast<long long>(blockIdx.x + 1) * a.units / a.grid;
-    const int nu = static_cast<int>(u1 - u0);
-    const int t_first = static_cast<int>(u0 / a.ppr);
-    const int t_last = static_cast<int>((u1 - 1) / a.ppr);
+    const int u0 = static_cast<int>(blockIdx.x * a.units / static_cast<uint32_t>(a.grid));
+    const int u1 = static_cast<int>((blockIdx.x + 1) * a.units / static_cast<uint32_t>(a.grid));
+    const int nu = u1 - u0;
+    const int t_first = u0 / a.ppr;
+    const int t_last = (u1 - 1) / a.ppr;
 
     if (tid < S) {
         mbar_init(&full[tid], 1);
@@ -369,7 +387,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------- producer ----------------
         if (lane == 0) {
 #pragma unroll
-            for (int m = 0; m < 4; ++m)
+            for (int m = 0; m < 3; ++m)
                 asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.box[m])) : "memory");
             const uint64_t policy = policy_evict_first();
             const int early = a.prefetch < S ? a.prefetch : S;
@@ -446,14 +464,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         float v = 0.f;
 #pragma unroll
         for (int w = 0; w < kWarps; ++w) v += part[(ts * kWarps + w) * 32 + lane];
-        const long long tb = static_cast<long long>(t) * a.ppr, te = tb + a.ppr;
+        const int tb = t * a.ppr, te = tb + a.ppr;
         const int row = t * kTileRows + lane;
         if (tb < u0) {
             st_relaxed(a.slot + static_cast<size_t>(blockIdx.x) * 32 + lane, kPresent | __float_as_uint(v));
             return;
         }
         if (te > u1) {
-            const int last = cta_of(te - 1, a.units, a.grid);
+            const int last = cta_of(static_cast<uint32_t>(te - 1), a.units, a.grid);
             for (int j0 = blockIdx.x + 1; j0 <= last; j0 += 4) {
                 unsigned long long wv[4];
 #pragma unroll
@@ -513,8 +531,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // this CTA's range in pair coordinates: first/last row tile, where the
     // range starts in the first one and ends in the last one, and the boxes
     // of the first segment and of a full row
-    const int p_first = static_cast<int>(u0 - static_cast<long long>(t_first) * a.ppr);
-    const int p_end = static_cast<int>(u1 - static_cast<long long>(t_last) * a.ppr);
+    const int p_first = u0 - t_first * a.ppr;
+    const int p_end = u1 - t_last * a.ppr;
     const int boxes_first = boxes_in((t_first == t_last ? p_end : a.ppr) - p_first);
     const int boxes_row = boxes_in(a.ppr);
     int tile = t_first, p = p_first + warp;
@@ -524,7 +542,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int before = tile == t_first ? 0 : boxes_first + (tile - t_first - 1) * boxes_row;
         const BoxPos bp = box_of(p, s0, s1, before);
         const int j = bp.box, q = bp.q, width = bp.width;
-        const int s = j & (S - 1);
+        const int s = j % S;
         // wait until the stage holds box j, then for its bytes
         if (seqno[s] != j) {
             bool ok = true;
@@ -607,7 +625,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 struct Q4MmaPlan {
-    int grid, tiles, ppr, max_tiles;
+    int grid, tiles, ppr, max_tiles, stages;
     long long units;
     size_t smem;
 };
@@ -618,11 +636,17 @@ bool q4_mma_plan(Q4MmaPlan &p, int k, int n, const DeviceInfo &dev) {
     p.ppr = k / 256;
     p.units = static_cast<long long>(p.tiles) * p.ppr;
     p.grid = static_cast<int>(p.units < dev.sm_count ? p.units : dev.sm_count);
+    if (p.units * (p.grid + 1) >= (1ll << 32)) return false;  // the kernel's index math is 32-bit
     const long long per = (p.units + p.grid - 1) / p.grid;
     p.max_tiles = static_cast<int>((per + p.ppr - 1) / p.ppr + 1);
-    p.smem = static_cast<size_t>(kStages) * kStageBytes + static_cast<size_t>(k / 128) * kRecBytes +
-             sizeof(float) * p.max_tiles * kWarps * 32 + 16 * kStages + 8 * kStages + 4 * p.max_tiles + 16;
-    return p.smem + 1024 <= static_cast<size_t>(dev.smem_optin);
+    // each stage held by a consumer warp for ~a pair's compute time while the
+    // next boxes are in flight: the deeper the ring, the less the warps wait
+    for (p.stages = kMaxStages; p.stages >= kMinStages; --p.stages) {
+        p.smem = static_cast<size_t>(p.stages) * kStageBytes + static_cast<size_t>(k / 128) * kRecBytes +
+                 sizeof(float) * p.max_tiles * kWarps * 32 + 24 * p.stages + 4 * p.max_tiles + 16;
+        if (p.smem + 1024 <= static_cast<size_t>(dev.smem_optin)) return true;
+    }
+    return false;
 }
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
@@ -701,7 +725,7 @@ cudaError_t launch_q4_mma_gemv(const GemvRequest &r, const DeviceInfo &dev, cuda
     a.y = r.y;
     a.slot = static_cast<unsigned long long *>(r.fixup);
     a.err = dev.err;
-    a.units = p.units;
+    a.units = static_cast<uint32_t>(p.units);
     a.k = r.k;
     a.n = r.n;
     a.tiles = p.tiles;
@@ -709,6 +733,7 @@ cudaError_t launch_q4_mma_gemv(const GemvRequest &r, const DeviceInfo &dev, cuda
     a.grid = p.grid;
     a.prefetch = r.prefetch_weights ? 1 << 30 : 0;
     a.max_tiles = p.max_tiles;
+    a.stages = p.stages;
     static int configured[64] = {0};
     int devno = 0;
     cudaGetDevice(&devno);
