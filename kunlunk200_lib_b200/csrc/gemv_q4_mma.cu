@@ -34,7 +34,9 @@
 //    holds one box; before waiting on a stage's mbarrier a warp checks the
 //    box sequence number the producer stored for the stage (a warp may run
 //    several boxes ahead, and an mbarrier parity alone only tells adjacent
-//    phases apart), and the last warp to finish a box's pairs releases it;
+//    phases apart).  A stage's "empty" mbarrier counts five arrivals: one
+//    per pair from the warp that computed it, and the producer's for the
+//    pairs a narrower box lacks;
 //  * within a pair a warp computes two m16 tiles (rows 0-15 and 16-31) per
 //    group.  For group q the four blocks use the four column pairs of the
 //    n8 MMA: column pair i holds (hi, lo) of block beta(i)'s activations and
@@ -46,11 +48,13 @@
 //    memory (544 bytes per group: the B fragments of the four column pairs,
 //    16 zero bytes and the four block scales), so the main loop reads them
 //    with one 16-byte load per block;
-//  * a row tile is finished by the last of the CTA's warps to arrive at it:
-//    it sums the warps' partials in warp order and stores Y, or, for a tile
-//    shared with other CTAs, publishes its sum (if a lower CTA holds the
-//    tile's first pairs) or collects the higher CTAs' published sums in CTA
-//    order before storing Y, so results do not depend on timing.
+//  * each warp leaves its partial sums of each row tile in shared memory;
+//    after the last pair the CTA's warps meet at one barrier and finish the
+//    CTA's tiles (one warp per tile): sum the warps' partials in warp order
+//    and store Y, or, for a tile shared with other CTAs, publish the sum (if
+//    a lower CTA holds the tile's first pairs) or collect the higher CTAs'
+//    published sums in CTA order before storing Y, so results do not depend
+//    on timing.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -362,8 +366,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *full = reinterpret_cast<uint64_t *>(part + a.max_tiles * kWarps * 32);
     uint64_t *empty = full + S;
     volatile int *seqno = reinterpret_cast<volatile int *>(empty + S);  // box held by each stage
-    int *done = const_cast<int *>(seqno) + S;                          // pairs finished per stage
-    int *tcnt = done + S;                                               // [max_tiles] warp arrivals
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int u0 = static_cast<int>(blockIdx.x * a.units / static_cast<uint32_t>(a.grid));
@@ -374,12 +376,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (tid < S) {
         mbar_init(&full[tid], 1);
-        mbar_init(&empty[tid], 1);
+        mbar_init(&empty[tid], kMaxBoxPairs);  // one arrival per pair slot of a box
         fence_mbar_init();
         seqno[tid] = -1;
-        done[tid] = 0;
     }
-    if (tid < a.max_tiles) tcnt[tid] = 0;
     __syncthreads();
     pdl_launch_dependents();
 
@@ -400,6 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_arrive_expect_tx(&full[s], kTileRows * kPairBytes * bw.width);
                 tma_load_2d(ring_u + s * kStageBytes, &maps.box[map_of_width(bw.width)], bw.pair * kPairWords,
                             bw.tile * kTileRows, &full[s], policy);
+                if (bw.width < kMaxBoxPairs) mbar_arrive_count(&empty[s], kMaxBoxPairs - bw.width);
                 if (++s == S) { s = 0; phase ^= 1; }
             }
             if (j <= early) pdl_wait_prior();
@@ -496,21 +497,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (row < a.n) a.y[row] = v;
     };
-    auto arrive = [&](int ts) {
-        __syncwarp();
-        int last = 0;
-        if (lane == 0) {
-            __threadfence_block();
-            last = atomicAdd(&tcnt[ts], 1) == kWarps - 1;
-            __threadfence_block();
-        }
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (last) finish_tile(ts);
-    };
 
     const uint32_t ring_u = smem_u32(ring), xrec_u = smem_u32(xrec);
     float acc[4] = {0.f, 0.f, 0.f, 0.f};  // rows g, g+8, g+16, g+24 of the current tile
-    int cur = -1, next_arrival = t_first;
+    int cur = -1;
     auto flush = [&](int t) {
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
@@ -524,8 +514,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
 #pragma unroll
         for (int r = 0; r < 4; ++r) acc[r] = 0.f;
-        arrive(t - t_first);
-        next_arrival = t + 1;
     };
 
     // this CTA's range in pair coordinates: first/last row tile, where the
@@ -555,7 +543,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&full[s], (j / S) & 1, a.err, kErrBulkTimeout)) break;
         if (tile != cur) {
             if (cur >= 0) flush(cur);
-            for (; next_arrival < tile; ++next_arrival) arrive(next_arrival - t_first);
             cur = tile;
         }
         const uint32_t pitch = kPairBytes * width;
@@ -605,23 +592,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             acc[2] = fmaf(s2, d1[0] + d1[1], acc[2]);
             acc[3] = fmaf(s3, d1[2] + d1[3], acc[3]);
         }
-        // the last warp to finish a pair of this box releases the stage; the
-        // proxy fence orders this warp's reads before the next TMA write into it
+        // release this pair's slot of the stage; the proxy fence orders this
+        // warp's reads before the next TMA write into it
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
-        if (lane == 0) {
-            __threadfence_block();
-            if (atomicAdd(&done[s], 1) == width - 1) {
-                __threadfence_block();
-                done[s] = 0;
-                mbar_arrive(&empty[s]);
-            }
-        }
+        if (lane == 0) mbar_arrive(&empty[s]);
         p += kWarps;
         while (p >= a.ppr) { p -= a.ppr; ++tile; }
     }
     if (cur >= 0) flush(cur);
-    for (; next_arrival <= t_last; ++next_arrival) arrive(next_arrival - t_first);
+    consumer_sync();  // every warp's partials are in shared memory
+    for (int ts = warp; ts <= t_last - t_first; ts += kWarps) finish_tile(ts);
 }
 
 struct Q4MmaPlan {
@@ -643,7 +624,7 @@ bool q4_mma_plan(Q4MmaPlan &p, int k, int n, const DeviceInfo &dev) {
     // next boxes are in flight: the deeper the ring, the less the warps wait
     for (p.stages = kMaxStages; p.stages >= kMinStages; --p.stages) {
         p.smem = static_cast<size_t>(p.stages) * kStageBytes + static_cast<size_t>(k / 128) * kRecBytes +
-                 sizeof(float) * p.max_tiles * kWarps * 32 + 24 * p.stages + 4 * p.max_tiles + 16;
+                 sizeof(float) * p.max_tiles * kWarps * 32 + 20 * p.stages + 16;
         if (p.smem + 1024 <= static_cast<size_t>(dev.smem_optin)) return true;
     }
     return false;
