@@ -48,13 +48,41 @@ __device__ __forceinline__ uint32_t block_max(uint32_t v, uint32_t *scratch) {
 }
 
 // ---- a8 tensor: one CTA for small tensors ---------------------------------
+// Three passes over X (max|x|; q0 and max|r|; q1).  With X 16-byte aligned
+// and count % 4 == 0 each thread reads float4s eight at a time, so a pass
+// costs a few memory latencies rather than one per element.
+__device__ __forceinline__ void a8_q0(float v, float inv0, float step0, int &q0, uint32_t &rbits) {
+    q0 = round_away_127(__fmul_rn(v, inv0));
+    rbits = abs_bits(__fsub_rn(v, __fmul_rn(static_cast<float>(q0), step0)));
+}
+
 __global__ void __launch_bounds__(1024) a8_single_kernel(const float *x, size_t count, int8_t *q, float *maxima,
                                                          int *err) {
     __shared__ uint32_t scratch[32];
+    const bool vec = (count % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(q) & 3) == 0);
+    const size_t count4 = vec ? count / 4 : 0;
+    const float4 *x4 = reinterpret_cast<const float4 *>(x);
+    constexpr int U = 8;
     uint32_t m = 0;
     bool bad = false;
-    for (size_t j = threadIdx.x; j < count; j += blockDim.x) {
-        uint32_t u = abs_bits(x[j]);
+    // pass 1: max |x|
+    for (size_t j0 = threadIdx.x; j0 < count4; j0 += U * blockDim.x) {
+        float4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const size_t j = j0 + u * blockDim.x;
+            v[u] = j < count4 ? __ldg(x4 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const uint32_t a = abs_bits(v[u].x), b = abs_bits(v[u].y), c = abs_bits(v[u].z), d = abs_bits(v[u].w);
+            bad |= (a >= 0x7f800000u) | (b >= 0x7f800000u) | (c >= 0x7f800000u) | (d >= 0x7f800000u);
+            m = max(m, max(max(a, b), max(c, d)));
+        }
+    }
+    for (size_t j = 4 * count4 + threadIdx.x; j < count; j += blockDim.x) {
+        const uint32_t u = abs_bits(x[j]);
         bad |= u >= 0x7f800000u;
         m = max(m, u);
     }
@@ -65,21 +93,69 @@ __global__ void __launch_bounds__(1024) a8_single_kernel(const float *x, size_t 
     const uint32_t m0 = block_max(m, scratch);
     const float max0 = m0 ? __uint_as_float(m0) : 1.0f;
     const float inv0 = __fdiv_rn(127.0f, max0), step0 = __fdiv_rn(max0, 127.0f);
+    // pass 2: q0 = round(x * 127 / max0), max |x - q0 * max0 / 127|
     m = 0;
-    for (size_t j = threadIdx.x; j < count; j += blockDim.x) {
-        const float v = x[j];
-        const int q0 = round_away_127(__fmul_rn(v, inv0));
+    for (size_t j0 = threadIdx.x; j0 < count4; j0 += U * blockDim.x) {
+        float4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const size_t j = j0 + u * blockDim.x;
+            v[u] = j < count4 ? __ldg(x4 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const size_t j = j0 + u * blockDim.x;
+            int a, b, c, d;
+            uint32_t ra, rb, rc, rd;
+            a8_q0(v[u].x, inv0, step0, a, ra);
+            a8_q0(v[u].y, inv0, step0, b, rb);
+            a8_q0(v[u].z, inv0, step0, c, rc);
+            a8_q0(v[u].w, inv0, step0, d, rd);
+            if (j < count4) {
+                reinterpret_cast<char4 *>(q)[j] =
+                    make_char4(static_cast<signed char>(a), static_cast<signed char>(b), static_cast<signed char>(c),
+                               static_cast<signed char>(d));
+                m = max(m, max(max(ra, rb), max(rc, rd)));
+            }
+        }
+    }
+    for (size_t j = 4 * count4 + threadIdx.x; j < count; j += blockDim.x) {
+        int q0;
+        uint32_t r;
+        a8_q0(x[j], inv0, step0, q0, r);
         q[j] = static_cast<int8_t>(q0);
-        const float r = __fsub_rn(v, __fmul_rn(static_cast<float>(q0), step0));
-        m = max(m, abs_bits(r));
+        m = max(m, r);
     }
     const uint32_t m1 = block_max(m, scratch);
     const float max1 = m1 ? __uint_as_float(m1) : 1.0f;
     const float inv1 = __fdiv_rn(127.0f, max1);
-    for (size_t j = threadIdx.x; j < count; j += blockDim.x) {
-        const float v = x[j];
-        const int q0 = q[j];
-        const float r = __fsub_rn(v, __fmul_rn(static_cast<float>(q0), step0));
+    // pass 3: q1 = round(r * 127 / max1), r recomputed from x and q0
+    for (size_t j0 = threadIdx.x; j0 < count4; j0 += U * blockDim.x) {
+        float4 v[U];
+        char4 c0[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const size_t j = j0 + u * blockDim.x;
+            v[u] = j < count4 ? __ldg(x4 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+            c0[u] = j < count4 ? reinterpret_cast<const char4 *>(q)[j] : make_char4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const size_t j = j0 + u * blockDim.x;
+            const float ra = __fsub_rn(v[u].x, __fmul_rn(static_cast<float>(c0[u].x), step0));
+            const float rb = __fsub_rn(v[u].y, __fmul_rn(static_cast<float>(c0[u].y), step0));
+            const float rc = __fsub_rn(v[u].z, __fmul_rn(static_cast<float>(c0[u].z), step0));
+            const float rd = __fsub_rn(v[u].w, __fmul_rn(static_cast<float>(c0[u].w), step0));
+            if (j < count4)
+                reinterpret_cast<char4 *>(q + count)[j] = make_char4(
+                    static_cast<signed char>(round_away_127(__fmul_rn(ra, inv1))),
+                    static_cast<signed char>(round_away_127(__fmul_rn(rb, inv1))),
+                    static_cast<signed char>(round_away_127(__fmul_rn(rc, inv1))),
+                    static_cast<signed char>(round_away_127(__fmul_rn(rd, inv1))));
+        }
+    }
+    for (size_t j = 4 * count4 + threadIdx.x; j < count; j += blockDim.x) {
+        const float r = __fsub_rn(x[j], __fmul_rn(static_cast<float>(q[j]), step0));
         q[count + j] = static_cast<int8_t>(round_away_127(__fmul_rn(r, inv1)));
     }
     if (threadIdx.x == 0) {
