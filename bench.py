@@ -19,6 +19,10 @@ GEMV.  Between timed steps the weights rotate through enough distinct sets
 that the whole rotation exceeds twice the L2 size, so every step streams its
 weights from HBM.
 
+--workload q4-gemm | f16-gemm | f32-gemm | i8-gemm [--batch B] measures BASELINE
+configs 2-4 instead (the batched matmul in TFLOP/s of the logical 2*N*K*batch
+work, with the HBM and tensor rooflines); the default, gemv, is config 1.
+
 --impl reference times the reference's CPU implementation of the same path
 (bench/native-q4-reference.h reference(), compiled from the reference sources
 into oracle/_ref; the C restatement in oracle/ when that is absent) on the
@@ -56,8 +60,9 @@ def read_peaks() -> dict:
     if os.path.exists(path):
         with open(path) as f:
             p = json.load(f)
-        return {"hbm_gbs": float(p["hbm_gbs"]), "source": "measured"}
-    return {"hbm_gbs": FALLBACK_HBM_GBS, "source": "fallback"}
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p.get("bf16_tflops", FALLBACK_BF16_TFLOPS)),
+                "source": "measured"}
+    return {"hbm_gbs": FALLBACK_HBM_GBS, "bf16_tflops": FALLBACK_BF16_TFLOPS, "source": "fallback"}
 
 
 def profile_traffic(name: str):
@@ -436,7 +441,7 @@ def run_ours(args) -> None:
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / peaks["hbm_gbs"],
                          "peak_source": peaks["source"],
-                         "traffic": profile_traffic("gemv_q4_0_k4096_n11008.md"),
+                         "traffic": profile_traffic("q4_mma_gemv_k4096_n11008.md"),
                          "kernel": "q4_mma_gemv_kernel",
                          "launch_us": launch_ms * 1e3,
                          "isolated_launch_us": {"up": mean_up * 1e3, "down": mean_down * 1e3},
@@ -457,6 +462,296 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# Batched workloads, selected with --workload
+# ---------------------------------------------------------------------------
+GEMM_CONFIGS = {
+    # workload: (weight type name, K, N, default batch, config label)
+    "q4-gemm": ("q4_0", 4096, 14336, 128, "config 2: q4_0 batched GEMM (prefill), batch in {16, 128, 512}"),
+    "f16-gemm": ("f16", 8192, 8192, 64, "config 3: f16 GEMV/GEMM, batch in {1, 64}"),
+    "f32-gemm": ("f32", 8192, 8192, 64, "config 3: f32 GEMV/GEMM, batch in {1, 64}"),
+    "i8-gemm": ("rowwise_i8", 8192, 28672, 256, "config 4: rowwise-int8 GEMM, batch in {1, 32, 256}"),
+}
+
+
+def gemm_shape(args):
+    wname, k, n, batch, label = GEMM_CONFIGS[args.workload]
+    return wname, args.k or k, args.n or n, args.batch or batch, label
+
+
+def gemm_weight_bytes(K, wname: str, k: int, n: int) -> int:
+    return {"q4_0": n * (k // 32) * 18, "f16": 2 * n * k, "f32": 4 * n * k}.get(wname) or K.packed_i8_size(k, n)
+
+
+def gemm_cpu_rate(wname: str, k: int, n: int, batch: int, seconds: float, sample_rows: int = 0):
+    """The reference's CPU arithmetic for the batched path on a row sample:
+    FP64 dots over the exactly decoded weights (bench/native-q4-reference.h
+    reference()) for f32/f16/q4_0 on all host cores, or the rowwise-int8
+    two-component integer dots and combine (src/k200.cpp:209-239) on one core.
+    Returns (TFLOP/s of the logical 2*n*k*batch work, cores, kind, sample)."""
+    import oracle as O
+
+    threads = os.cpu_count() or 1
+    rows = sample_rows or max(1, min(n, 64))
+    x = (O.normal(0x09200ABC, batch * k, 0.0, 1.0) if wname == "rowwise_i8"
+         else O.uniform(0x09200ABC, batch * k, -1.0, 1.0))
+    w = O.normal(0x7340D123, rows * k, 0.0, 0.02) if wname in ("q4_0", "rowwise_i8") else \
+        O.uniform(0x7340D123, rows * k, -1.0, 1.0)
+    if wname == "rowwise_i8":
+        wq, scales = O.i8_pack_rows(w, k, rows)
+        cores = 1
+
+        def run():
+            q0, q1, m0, m1 = O.a8_tensor(x)
+            O.i8_matmul(wq, scales, q0, q1, m0, m1, k, rows, batch)
+    else:
+        if wname == "q4_0":
+            dec = O.q4_0_dequantize(O.q4_0_quantize(w, rows, k), rows, k)
+        elif wname == "f16":
+            dec = O.f16(w).astype(np.float32)
+        else:
+            dec = w
+        cores = threads
+
+        def run():
+            O.reference_fp64(dec, x, k, rows, batch, threads)
+    run()
+    t0 = time.perf_counter()
+    done = 0
+    while True:
+        run()
+        done += 1
+        if time.perf_counter() - t0 >= seconds and done >= 2:
+            break
+    dt = time.perf_counter() - t0
+    kind = "port"
+    sample = (f"{done} calls of {rows} weight rows x K{k} x batch {batch} "
+              f"({'int8 dots + combine' if wname == 'rowwise_i8' else 'FP64 reference() over decoded weights'}), "
+              f"{dt:.1f} s")
+    return 2.0 * rows * k * batch * done / dt / 1e12, cores, kind, sample
+
+
+def run_gemm(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    import kunlunk200_lib_b200 as K
+    from kunlunk200_lib_b200.shard import row_shard
+
+    wname, k, n, batch, label = gemm_shape(args)
+    wtype = {"q4_0": K.Q4_0, "f16": K.F16, "f32": K.F32, "rowwise_i8": K.ROWWISE_I8}[wname]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
+    if n % world:
+        raise SystemExit(f"N={n} does not split evenly over {world} GPUs")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dev = local
+    K.select(dev)
+    stream = torch.cuda.Stream()
+    K.set_stream(dev, stream.cuda_stream)
+    K.set_static_weights(dev, True)
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    n_sh = row_shard(n, world, rank)[1]
+    shard_bytes = gemm_weight_bytes(K, wname, k, n_sh)
+    sets = max(2, math.ceil(2 * l2 / shard_bytes) + 1)
+    gen = torch.Generator(device="cuda")
+    weights = []
+    with torch.cuda.stream(stream):
+        for s_ in range(sets):
+            gen.manual_seed(1000003 * s_ + 104729 * rank + 5)
+            if wname in ("q4_0", "rowwise_i8"):
+                w = torch.randn((n_sh, k), generator=gen, device="cuda", dtype=torch.float32) * 0.02
+            else:
+                w = torch.rand((n_sh, k), generator=gen, device="cuda", dtype=torch.float32) * 2 - 1
+            if wname == "q4_0":
+                W = torch.empty(shard_bytes, dtype=torch.uint8, device="cuda")
+                K.quantize_q4_0(dev, W, w, k, n_sh)
+            elif wname == "rowwise_i8":
+                W = torch.empty(shard_bytes, dtype=torch.uint8, device="cuda")
+                K.pack_i8_rows_device(dev, W, k, n_sh, 0, n_sh, w)
+            elif wname == "f16":
+                W = w.half()
+            else:
+                W = w
+            del w
+            weights.append(W)
+        gen.manual_seed(0x09200ABC)
+        if wname == "rowwise_i8":
+            x = torch.randn((batch, k), generator=gen, device="cuda", dtype=torch.float32)
+        else:
+            x = torch.rand((batch, k), generator=gen, device="cuda", dtype=torch.float32) * 2 - 1
+        y_sh = torch.empty((batch, n_sh), device="cuda")
+        y_full = y_sh if world == 1 else torch.empty((world, batch, n_sh), device="cuda")
+    stream.synchronize()
+    kern = K.Kernel()
+    i8 = wname == "rowwise_i8"
+
+    def step(s_: int):
+        W = weights[s_ % sets]
+        sc = K.packed_i8_scales(W, k, n_sh) if i8 else None
+        mx = K.packed_i8_maxima(W, k, n_sh) if i8 else None
+        K.matmul(kern, dev, y_sh, W, x, k, n_sh, batch, wtype, sc, mx)
+        if world > 1:
+            dist.all_gather_into_tensor(y_full, y_sh)
+
+    with torch.cuda.stream(stream):
+        for i in range(max(3, args.warmup)):
+            step(i)
+    stream.synchronize()
+    K.check(K.wait())
+    per_graph = sets * max(1, 24 // sets)
+    reps, rem = divmod(args.steps, per_graph)
+
+    def capture(nsteps: int):
+        if nsteps == 0:
+            return None
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(nsteps):
+                step(i)
+        return g
+
+    g_main, g_rem = (capture(per_graph) if reps else None), capture(rem)
+    with torch.cuda.stream(stream):
+        if g_main is not None:
+            g_main.replay()
+        if g_rem is not None:
+            g_rem.replay()
+    stream.synchronize()
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    phys = int(visible.split(",")[dev]) if visible and visible.split(",")[dev].strip().isdigit() else dev
+    clocks = ClockSampler(phys)
+    if rank == 0:
+        clocks.start()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    if rank == 0:
+        clocks.mark(True)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(reps):
+            g_main.replay()
+        if g_rem is not None:
+            g_rem.replay()
+        end.record(stream)
+    stream.synchronize()
+    torch.cuda.synchronize()
+    if rank == 0:
+        clocks.mark(False)
+    if world > 1:
+        dist.barrier()
+    t = torch.tensor([start.elapsed_time(end)], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    clock_info = clocks.stop() if rank == 0 else None
+    flops_step = 2.0 * n * k * batch
+    value = flops_step * args.steps / (ms * 1e-3) / 1e12
+    ms_step = ms / args.steps
+    # kernels of ours per matmul: the activation preparation (f16/q4_0 hi/lo
+    # split; rowwise-int8 quantiser: one CTA up to 64K elements, else three
+    # passes) and the matmul kernel itself
+    tc = batch >= 4 and k % 16 == 0 and (wname != "q4_0" or k % 256 == 0) and wname != "f32"
+    prep = (1 if (tc and wname in ("q4_0", "f16")) else 0) + ((1 if batch * k <= 65536 else 3) if i8 else 0)
+    launches = args.steps * (1 + prep)
+    peaks = read_peaks()
+    hbm_gbs = shard_bytes / (ms_step * 1e-3) / 1e9
+    tflops_gpu = flops_step / world / (ms_step * 1e-3) / 1e12
+    tensor_peak = peaks["bf16_tflops"] * (2 if i8 else 1)
+    hbm_frac, tensor_frac = hbm_gbs / peaks["hbm_gbs"], tflops_gpu / tensor_peak
+    bound = "tensor" if tensor_frac > hbm_frac else "hbm"
+    roof = {"bound": bound,
+            "achieved": tflops_gpu if bound == "tensor" else hbm_gbs,
+            "peak": tensor_peak if bound == "tensor" else peaks["hbm_gbs"],
+            "unit": "TFLOP/s" if bound == "tensor" else "GB/s",
+            "frac": tensor_frac if bound == "tensor" else hbm_frac,
+            "hbm": {"achieved": hbm_gbs, "frac": hbm_frac},
+            "tensor": {"achieved": tflops_gpu, "frac": tensor_frac,
+                       "peak_note": ("2x measured bf16 (dense int8 rate)" if i8 else "measured bf16")},
+            "peak_source": peaks["source"], "traffic": None,
+            "kernel": {"q4_0": "gemm_q4_kernel", "f16": "gemm_f16_kernel", "f32": "gemv_stream_kernel",
+                       "rowwise_i8": "gemm_i8_kernel"}[wname] if tc or wname == "f32" else "gemv_stream_kernel",
+            "launch_us": ms_step * 1e3}
+    # end to end through the C ABI: pinned host X in, pinned host Y out, every step
+    e2e_steps = min(args.steps, 500)
+    xh = torch.empty((batch, k), dtype=torch.float32).pin_memory()
+    xh.copy_(x.cpu())
+    yh = torch.empty(y_full.numel(), dtype=torch.float32).pin_memory()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for i in range(e2e_steps):
+            K.check(K.copy_async(x, xh, xh.numel() * 4, K.HOST_TO_DEVICE))
+            step(i)
+            K.check(K.copy_async(yh, y_full, yh.numel() * 4, K.DEVICE_TO_HOST))
+            K.check(K.wait())
+        e1.record(stream)
+    stream.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1)], device="cuda")
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = flops_step * e2e_steps / (float(te.item()) * 1e-3) / 1e12
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, cores, kind, sample = gemm_cpu_rate(wname, k, n, batch, 10.0)
+        cpu = {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": kind, "sample": sample}
+    if rank == 0:
+        unit = "TOP/s" if i8 else "TFLOP/s"
+        line = {
+            "metric": f"{wname}_batched_matmul_tflops", "value": value, "unit": unit, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": {"q4_0": "f16 hi/lo x f16 hi/lo", "f16": "f16 x f16 hi/lo",
+                                                                "f32": "f32", "rowwise_i8": "int8"}[wname],
+            "data": "synthetic",
+            "config": {"workload": f"{wname} matmul K{k} N{n} batch {batch} ({label})", "k": k, "n": n, "batch": batch,
+                       "parallelism": f"row-shard{world}+allgather" if world > 1 else "single",
+                       "work": "logical 2*N*K*batch per step",
+                       "l2": f"{sets} rotating weight sets ({sets * shard_bytes / 1e6:.0f} MB per GPU)",
+                       "timing": "CUDA graph replays, CUDA events on the launching stream, max over ranks"},
+            "roofline": roof, "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": unit, "h2d_bytes_per_step": xh.numel() * 4,
+                    "d2h_bytes_per_step": yh.numel() * 4, "steps": e2e_steps,
+                    "path": "k200_copy_async H2D + k200_matmul + k200_copy_async D2H + k200_wait per step"},
+            "gpu_launches": launches, "clocks": clock_info,
+        }
+        print(json.dumps(line), flush=True)
+    K.set_stream(dev, None)
+    del g_main, g_rem
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_gemm_reference(args) -> None:
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    wname, k, n, batch, label = gemm_shape(args)
+    import oracle as O  # noqa: F401  (the reference CPU arithmetic lives in the oracle)
+
+    per_step = 120.0 / max(1, args.steps + args.warmup)
+    value, cores, kind, sample = gemm_cpu_rate(wname, k, n, batch, max(0.05, per_step) * args.steps)
+    unit = "TOP/s" if wname == "rowwise_i8" else "TFLOP/s"
+    line = {"impl": "reference", "metric": f"{wname}_batched_matmul_tflops", "value": value, "unit": unit,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f64" if wname != "rowwise_i8" else "int8",
+            "data": "synthetic", "config": {"workload": f"{wname} matmul K{k} N{n} batch {batch} ({label})"},
+            "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": kind, "sample": sample},
+            "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -464,10 +759,19 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=200)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["gemv"] + sorted(GEMM_CONFIGS), default="gemv",
+                    help="gemv: config 1 (the metric's workload, default); others: BASELINE configs 2-4")
+    ap.add_argument("--batch", type=int, default=0, help="batched workloads: activation columns")
+    ap.add_argument("--k", type=int, default=0, help="batched workloads: override K")
+    ap.add_argument("--n", type=int, default=0, help="batched workloads: override N")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.workload != "gemv":
+        if args.steps == 100000:
+            args.steps = 200
+        run_gemm_reference(args) if args.impl == "reference" else run_gemm(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -216,6 +216,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1) gemm_i8_kernel(const __grid_con
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             const uint32_t idesc = instr_desc(2, 1, 1, kTileM, a.nb);  // s32 <- s8 x s8
+            // the two activation components are adjacent nb-row tiles: one 2nb-wide MMA when it fits
+            const bool merged = 2 * a.nb <= 256;
+            const uint32_t idesc2 = instr_desc(2, 1, 1, kTileM, merged ? 2 * a.nb : a.nb);
             for (int ks = 0; ks < a.ksteps; ++ks) {
                 const int s = ks % a.stages;
                 if (!mbar_wait(&full[s], (ks / a.stages) & 1, a.err, kErrBulkTimeout)) break;
@@ -225,8 +228,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1) gemm_i8_kernel(const __grid_con
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {  // 4 x 32 bytes of K per 128-byte step: +2 in the address field
                     const uint32_t acc = (ks | kk) != 0;
-                    mma_i8(taddr, da + 2 * kk, db0 + 2 * kk, idesc, acc);
-                    mma_i8(taddr + a.nb, da + 2 * kk, db1 + 2 * kk, idesc, acc);
+                    if (merged) {
+                        mma_i8(taddr, da + 2 * kk, db0 + 2 * kk, idesc2, acc);
+                    } else {
+                        mma_i8(taddr, da + 2 * kk, db0 + 2 * kk, idesc, acc);
+                        mma_i8(taddr + a.nb, da + 2 * kk, db1 + 2 * kk, idesc, acc);
+                    }
                 }
                 mma_commit(&empty[s]);  // frees the stage once these MMAs have read it
             }
@@ -322,13 +329,14 @@ __global__ void __launch_bounds__(kThreadsTc, 1) gemm_f16_kernel(const __grid_co
         __syncwarp();
     } else if (warp == 1) {
         if (lane == 0) {
-            const uint32_t idesc = instr_desc(1, 0, 0, kTileM, NB);  // f32 <- f16 x f16
+            // f32 <- f16 x f16; x hi and x lo are adjacent NB-row tiles: one 2NB-wide MMA
+            const uint32_t idesc = instr_desc(1, 0, 0, kTileM, 2 * NB);
             bool ok = true;
             for (int c = 0; c < nchunks && ok; ++c) {
                 const int slot = c & 1;
                 if (c >= 2 && !mbar_wait(&tfree[slot], ((c >> 1) - 1) & 1, a.err, kErrMmaTimeout)) break;
                 tc_fence_after();
-                const uint32_t d = taddr + slot * NB;
+                const uint32_t d = taddr + slot * 2 * NB;  // [W*x hi | W*x lo]
                 const int ks_end = min(a.ksteps, (c + 1) * kChunkSteps);
                 for (int ks = c * kChunkSteps; ks < ks_end; ++ks) {
                     const int s = ks % a.stages;
@@ -336,12 +344,10 @@ __global__ void __launch_bounds__(kThreadsTc, 1) gemm_f16_kernel(const __grid_co
                     tc_fence_after();
                     const uint32_t st = base + s * stage_bytes;
                     const uint64_t da = sw128_desc(st);
-                    const uint64_t db0 = sw128_desc(st + a_total), db1 = sw128_desc(st + a_total + b_bytes);
+                    const uint64_t db = sw128_desc(st + a_total);
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {
-                        mma_f16(d, da + 2 * kk, db0 + 2 * kk, idesc, (ks != c * kChunkSteps) || kk != 0);
-                        mma_f16(d, da + 2 * kk, db1 + 2 * kk, idesc, 1);
-                    }
+                    for (int kk = 0; kk < 4; ++kk)
+                        mma_f16(d, da + 2 * kk, db + 2 * kk, idesc, (ks != c * kChunkSteps) || kk != 0);
                     mma_commit(&empty[s]);
                 }
                 mma_commit(&tfull[slot]);
@@ -361,12 +367,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1) gemm_f16_kernel(const __grid_co
             if (!mbar_wait(&tfull[slot], (c >> 1) & 1, a.err, kErrMmaTimeout)) { ok = false; break; }
             tc_fence_after();
 #pragma unroll
-            for (int c0 = 0; c0 < NB; c0 += 16) {
+            for (int c0 = 0; c0 < 2 * NB; c0 += 16) {
                 uint32_t p[16];
-                tmem_ld16(lane_addr + slot * NB + c0, p);
+                tmem_ld16(lane_addr + slot * 2 * NB + c0, p);
                 tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < 16; ++i) sum[c0 + i] = __fadd_rn(sum[c0 + i], __uint_as_float(p[i]));
+                for (int i = 0; i < 16; ++i) sum[(c0 % NB) + i] = __fadd_rn(sum[(c0 % NB) + i], __uint_as_float(p[i]));
             }
             tc_fence_before();
             __syncwarp();
@@ -758,8 +764,8 @@ cudaError_t launch_gemm_tc(const GemvRequest &r, const DeviceInfo &dev, cudaStre
     const long long row_bytes = i8 ? r.k : 2ll * r.k;  // bytes per row of the MMA operands
     a.ksteps = static_cast<int>((row_bytes + kStepBytes - 1) / kStepBytes);
     uint32_t cols = 32;
-    // i8: two accumulators; f16: two chunk slots; q4: two chunk slots of 2 x nb columns
-    while (cols < static_cast<uint32_t>((q4 ? 4 : 2) * a.nb)) cols <<= 1;
+    // i8: two accumulators; f16 and q4: two chunk slots of 2 x nb columns
+    while (cols < static_cast<uint32_t>((i8 ? 2 : 4) * a.nb)) cols <<= 1;
     a.tmem_cols = cols;
     const size_t stage = static_cast<size_t>(kTileM) * kStepBytes * (q4 ? 2 : 1) + 2 * static_cast<size_t>(a.nb) * kStepBytes;
     // q4: three raw slots while that leaves three operand stages, else two
