@@ -119,6 +119,49 @@ void k200_pack_i8_rows_device(int device, void *weights, int k, int rows, int fi
 int k200_matmul_i8_noalloc(int device, void *y, const void *w, const void *x, int k, int n, int batch,
                            const float *scales, const float *maxima);
 
+/* ---- native Q4 layout: k200.h:127-131,203-224; src/q4-layout.cpp:7-45;
+ *      src/k200.cpp:545-617 ------------------------------------------------- */
+/* type: 0 f32 input, 1 f16 input (kunlun::InputType values) */
+int k200_native_q4_layout_supported(int k, int n);           /* native_q4_layout_supported, q4-layout.cpp:7-9 */
+size_t k200_native_q4_size(int k, int n);                    /* native_q4_size, q4-layout.cpp:10-14 */
+int k200_pack_native_q4(void *destination, size_t bytes, const void *q4, int k, int n); /* host pack, q4-layout.cpp:15-37 */
+void k200_upload_native_q4(int device, void *weights, const void *q4, int k, int n);   /* q4-layout.cpp:38-44 */
+const char *k200_native_q4_reason(int k, int n, int batch, int type);                  /* k200.cpp:545-552 */
+void *k200_native_q4_workspace_create(void);                 /* NativeQ4Workspace::NativeQ4Workspace */
+void k200_native_q4_workspace_destroy(void *workspace);      /* NativeQ4Workspace::~NativeQ4Workspace */
+/* out = {accelerated, fallback, hbm_workspace_bytes, l3_workspace_bytes} */
+void k200_native_q4_statistics(void *workspace, size_t out[4]);  /* NativeQ4Workspace::statistics */
+/* Completes before returning; 1: W4A8x2 path, 0: exact FP32 fallback. */
+int k200_native_q4_matmul(void *workspace, int device, void *y, const void *weights, const void *input, int k, int n,
+                          int batch, int type);              /* native_q4_matmul, k200.cpp:553-617 */
+
+/* ---- common Q4 ABI v1: k200.h:226-335; src/q4-common.inc:1-334 ----------- */
+typedef struct {
+    uint32_t abi_version, quant_type, layout, scale_order;
+    int k, n, kp, np, device;
+    size_t scale_offset, payload_bytes;
+} k200_common_q4_info;                                       /* kunlun::CommonQ4Info */
+int k200_common_q4_supported(int k, int n);                  /* q4-common.inc:4 */
+size_t k200_common_q4_size(int k, int n);                    /* q4-common.inc:5-8 */
+/* Host pack of n rows of Q4_0 blocks into the payload (the packing
+ * k200_common_q4_weight_upload performs; src/q4-common-pack.h:34-41).  No
+ * device work; 1 on success, 0 on a bad shape or buffer size. */
+int k200_common_q4_pack(const void *q4, size_t bytes, int k, int n, void *out, size_t out_bytes);
+void *k200_common_q4_weight_create(int device, int k, int n, void *storage, size_t bytes); /* q4-common.inc:16-25 */
+void k200_common_q4_weight_destroy(void *weight);
+void k200_common_q4_weight_upload(void *weight, const void *q4, size_t bytes);          /* q4-common.inc:32-44 */
+void *k200_common_q4_weight_data(void *weight);
+void k200_common_q4_weight_info(void *weight, k200_common_q4_info *out);
+void *k200_common_q4_workspace_create(void);
+void k200_common_q4_workspace_destroy(void *workspace);
+/* X [m,k] (type 0 f32, 1 f16), Y [m,n] f32; completes before returning. */
+void k200_common_q4_matmul(void *workspace, int device, void *y, const void *weight, const void *input, int m,
+                           int type);                        /* common_q4_matmul, q4-common.inc:319-334 */
+/* The last call's quantised activations: *values, *scales, out = {rows, kp, components}. */
+void k200_common_q4_quantization(void *workspace, const void **values, const void **scales, int out[3]);
+/* out = {paths[0..7], calls, chunks} */
+void k200_common_q4_statistics(void *workspace, size_t out[10]);
+
 #ifdef __cplusplus
 }
 #endif

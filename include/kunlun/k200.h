@@ -15,6 +15,10 @@
 //   rowwise int8       k200.h:90-96    aligned packed_i8_size/_scales/_maxima upload_i8_rows
 //   matmul             k200.h:98-105
 //   elementwise        k200.h:106-107
+//   native Q4 layout   k200.h:127-131,203-224  native_q4_* NativeQ4Workspace
+//   common Q4 ABI v1   k200.h:226-335  CommonQ4Weight CommonQ4Workspace
+//                                      common_q4_matmul (not the activation
+//                                      lease / shared / pair calls)
 //   statistics/version k200.h:345-350
 //
 // Device model: a "PD" index is a CUDA device ordinal (0..7 on an 8-GPU box).
@@ -112,6 +116,110 @@ void matmul(Kernel &, int device, void *y, const void *w, const void *x, int k, 
 // rms_norm normalises rows of `width`.  Completes before returning.
 void elementwise(Kernel &, int device, void *y, const void *a, const void *b, int count, int width, int b_count,
                  ElementwiseOp op, float parameter = 0);
+
+// ---- native Q4 layout (reference k200.h:127-131, 203-224) ------------------
+// The original Q4_0 values and FP16 block scales, N padded to 32:
+// [N32 tile][K32 block][16 byte pairs][32 rows] of signed 4-bit pairs, then the
+// scales.  Packing runs on the host.
+bool native_q4_layout_supported(int k, int n);
+size_t native_q4_size(int k, int n);
+bool pack_native_q4(void *destination, size_t bytes, const void *q4, int k, int n);
+void upload_native_q4(int device, void *weights, const void *q4, int k, int n);
+// Empty string: the W4A8x2 path applies (batch 1, N % 128 == 0, ...).
+const char *native_q4_reason(int k, int n, int batch, InputType type);
+struct NativeQ4Statistics {
+    size_t accelerated, fallback;
+    size_t hbm_workspace_bytes, l3_workspace_bytes;
+};
+class NativeQ4Workspace {
+public:
+    NativeQ4Workspace();
+    ~NativeQ4Workspace();
+    NativeQ4Workspace(const NativeQ4Workspace &) = delete;
+    NativeQ4Workspace &operator=(const NativeQ4Workspace &) = delete;
+    NativeQ4Statistics statistics() const;
+    struct Impl;
+private:
+    Impl *impl_;
+    friend bool native_q4_matmul(NativeQ4Workspace &, int, void *, const void *, const void *, int, int, int,
+                                 InputType);
+};
+// Completes before returning.  True: W4A8x2 (two-component per-tensor int8
+// activations); false: the exact FP32 fallback.  Y [batch,n] f32, X [batch,k].
+bool native_q4_matmul(NativeQ4Workspace &, int device, void *y, const void *weights, const void *input, int k, int n,
+                      int batch = 1, InputType type = InputType::f32);
+
+// ---- common Q4 ABI v1 (reference k200.h:226-335) --------------------------
+struct CommonQ4Info {
+    uint32_t abi_version, quant_type, layout, scale_order;
+    int k, n, kp, np, device;
+    size_t scale_offset, payload_bytes;
+};
+bool common_q4_supported(int k, int n);
+size_t common_q4_size(int k, int n);
+struct CommonQ4ActivationStatistics {
+    size_t prepare_calls, quantized_chunks, quant_kernel_launches;
+    size_t prepared_matmuls, prepared_chunks, invalidations, rejected_calls;
+    size_t hbm_activation_bytes;
+    uint64_t quantization_ns, preparation_ns;
+};
+class CommonQ4Workspace;
+struct CommonQ4WeightStatistics {
+    size_t uploads, upload_bytes;
+    double pack_ms, upload_ms;
+};
+class CommonQ4Weight {
+public:
+    // Borrowed storage must be 256-byte aligned; null storage allocates a Buffer.
+    CommonQ4Weight(int device, int k, int n, void *storage = nullptr, size_t bytes = 0);
+    ~CommonQ4Weight();
+    CommonQ4Weight(const CommonQ4Weight &) = delete;
+    CommonQ4Weight &operator=(const CommonQ4Weight &) = delete;
+    CommonQ4Info info() const;
+    CommonQ4WeightStatistics statistics() const;
+    void *data() const;
+    // Packs N rows of K/32 Q4_0 blocks on the host and uploads them.
+    void upload(const void *q4, size_t bytes);
+    struct Impl;
+private:
+    Impl *impl_;
+    friend void common_q4_matmul(class CommonQ4Workspace &, int, void *, const CommonQ4Weight &, const void *, int,
+                                 InputType);
+};
+struct CommonQ4Statistics {
+    // GEMV, Combined, Wide, Rows64, Rows128, Combo2, Combo4, exact CL.
+    size_t paths[8], calls, chunks;
+    size_t hbm_workspace_bytes, l3_workspace_bytes, slice_bytes;
+};
+struct CommonQ4MacStatistics {
+    size_t baseline_sd_calls, stream_sd_calls, shape_fallbacks, resident_l1d_bytes;
+};
+struct CommonQ4Quantization {
+    const void *values;
+    const void *scales;
+    int rows, kp, components;
+};
+class CommonQ4Workspace {
+public:
+    CommonQ4Workspace();
+    ~CommonQ4Workspace();
+    CommonQ4Workspace(const CommonQ4Workspace &) = delete;
+    CommonQ4Workspace &operator=(const CommonQ4Workspace &) = delete;
+    CommonQ4Statistics statistics() const;
+    CommonQ4ActivationStatistics activation_statistics() const;
+    CommonQ4MacStatistics mac_statistics() const;
+    // The last call's quantised activations (device buffers, valid until the next call).
+    CommonQ4Quantization quantization() const;
+    struct Impl;
+private:
+    Impl *impl_;
+    friend void common_q4_matmul(CommonQ4Workspace &, int, void *, const CommonQ4Weight &, const void *, int,
+                                 InputType);
+};
+// X [m,k], Y [m,n].  Completes before returning.  M = 1: two-component A8;
+// M > 1: one int8 scale per activation row (Row A8).
+void common_q4_matmul(CommonQ4Workspace &, int device, void *y, const CommonQ4Weight &, const void *input, int m,
+                      InputType type = InputType::f32);
 
 struct Statistics {
     size_t matmuls[2];            // devices 0 and 1 (ABI of the reference struct)

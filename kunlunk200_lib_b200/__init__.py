@@ -64,7 +64,36 @@ _SIGNATURES = {
     "k200_quantize_q4_0": (None, [C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int]),
     "k200_matmul_i8_noalloc": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
                                          C.c_void_p, C.c_void_p]),
+    # native Q4 layout
+    "k200_native_q4_layout_supported": (C.c_int, [C.c_int, C.c_int]),
+    "k200_native_q4_size": (C.c_size_t, [C.c_int, C.c_int]),
+    "k200_pack_native_q4": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p, C.c_int, C.c_int]),
+    "k200_upload_native_q4": (None, [C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int]),
+    "k200_native_q4_reason": (C.c_char_p, [C.c_int, C.c_int, C.c_int, C.c_int]),
+    "k200_native_q4_workspace_create": (C.c_void_p, []),
+    "k200_native_q4_workspace_destroy": (None, [C.c_void_p]),
+    "k200_native_q4_statistics": (None, [C.c_void_p, C.POINTER(C.c_size_t)]),
+    "k200_native_q4_matmul": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
+                                        C.c_int, C.c_int]),
+    # common Q4 ABI v1
+    "k200_common_q4_supported": (C.c_int, [C.c_int, C.c_int]),
+    "k200_common_q4_size": (C.c_size_t, [C.c_int, C.c_int]),
+    "k200_common_q4_pack": (C.c_int, [C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.c_void_p, C.c_size_t]),
+    "k200_common_q4_weight_create": (C.c_void_p, [C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_size_t]),
+    "k200_common_q4_weight_destroy": (None, [C.c_void_p]),
+    "k200_common_q4_weight_upload": (None, [C.c_void_p, C.c_void_p, C.c_size_t]),
+    "k200_common_q4_weight_data": (C.c_void_p, [C.c_void_p]),
+    "k200_common_q4_weight_info": (None, [C.c_void_p, C.c_void_p]),
+    "k200_common_q4_workspace_create": (C.c_void_p, []),
+    "k200_common_q4_workspace_destroy": (None, [C.c_void_p]),
+    "k200_common_q4_matmul": (None, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int]),
+    "k200_common_q4_quantization": (None, [C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
+                                           C.POINTER(C.c_int)]),
+    "k200_common_q4_statistics": (None, [C.c_void_p, C.POINTER(C.c_size_t)]),
 }
+
+# kunlun::InputType values (k200.h:132)
+INPUT_F32, INPUT_F16 = 0, 1
 
 
 def exported_symbols() -> list[str]:
@@ -302,6 +331,157 @@ def matmul_i8_noalloc(device: int, y, w, x, k: int, n: int, batch: int, scales, 
     """
     return lib().k200_matmul_i8_noalloc(device, _ptr(y), _ptr(w), _ptr(x), k, n, batch, _ptr(scales),
                                         _ptr(maxima))
+
+
+# ---------------------------------------------------------------------------
+# native Q4 layout (k200.h:127-131, 203-224)
+# ---------------------------------------------------------------------------
+def native_q4_layout_supported(k: int, n: int) -> bool:
+    return bool(lib().k200_native_q4_layout_supported(k, n))
+
+
+def native_q4_size(k: int, n: int) -> int:
+    return lib().k200_native_q4_size(k, n)
+
+
+def pack_native_q4(q4: np.ndarray, k: int, n: int) -> np.ndarray:
+    """Host pack of N rows of Q4_0 blocks into the native layout (raises if unsupported)."""
+    src = np.ascontiguousarray(q4, np.uint8)
+    out = np.empty(native_q4_size(k, n), np.uint8)
+    if not lib().k200_pack_native_q4(_ptr(out), out.nbytes, _ptr(src), k, n):
+        raise ValueError("native Q4 layout unsupported for this shape or buffer")
+    return out
+
+
+def upload_native_q4(device: int, weights, q4: np.ndarray, k: int, n: int) -> None:
+    src = np.ascontiguousarray(q4, np.uint8)
+    lib().k200_upload_native_q4(device, _ptr(weights), _ptr(src), k, n)
+
+
+def native_q4_reason(k: int, n: int, batch: int, type: int = INPUT_F32) -> str:
+    return lib().k200_native_q4_reason(k, n, batch, int(type)).decode()
+
+
+class NativeQ4Workspace:
+    """kunlun::NativeQ4Workspace (k200.h:205-216): scratch bound to one device."""
+
+    def __init__(self):
+        self.handle = lib().k200_native_q4_workspace_create()
+
+    def statistics(self) -> dict:
+        out = (C.c_size_t * 4)()
+        lib().k200_native_q4_statistics(self.handle, out)
+        return {"accelerated": out[0], "fallback": out[1], "hbm_workspace_bytes": out[2],
+                "l3_workspace_bytes": out[3]}
+
+    def close(self) -> None:
+        if self.handle:
+            lib().k200_native_q4_workspace_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def native_q4_matmul(workspace: NativeQ4Workspace, device: int, y, weights, x, k: int, n: int, batch: int = 1,
+                     type: int = INPUT_F32) -> bool:
+    """Completes before returning; True: W4A8x2 path, False: exact FP32 fallback."""
+    return bool(lib().k200_native_q4_matmul(workspace.handle, device, _ptr(y), _ptr(weights), _ptr(x), k, n,
+                                            batch, int(type)))
+
+
+# ---------------------------------------------------------------------------
+# common Q4 ABI v1 (k200.h:226-335)
+# ---------------------------------------------------------------------------
+class _CommonQ4Info(C.Structure):
+    _fields_ = [("abi_version", C.c_uint32), ("quant_type", C.c_uint32), ("layout", C.c_uint32),
+                ("scale_order", C.c_uint32), ("k", C.c_int), ("n", C.c_int), ("kp", C.c_int), ("np", C.c_int),
+                ("device", C.c_int), ("scale_offset", C.c_size_t), ("payload_bytes", C.c_size_t)]
+
+
+def common_q4_supported(k: int, n: int) -> bool:
+    return bool(lib().k200_common_q4_supported(k, n))
+
+
+def common_q4_size(k: int, n: int) -> int:
+    return lib().k200_common_q4_size(k, n)
+
+
+def common_q4_pack(q4: np.ndarray, k: int, n: int) -> np.ndarray:
+    """Host pack of N rows of Q4_0 blocks into the common ABI v1 payload."""
+    src = np.ascontiguousarray(q4, np.uint8)
+    out = np.empty(common_q4_size(k, n), np.uint8)
+    if not lib().k200_common_q4_pack(_ptr(src), src.nbytes, k, n, _ptr(out), out.nbytes):
+        raise ValueError("common Q4 layout unsupported for this shape or buffer")
+    return out
+
+
+class CommonQ4Weight:
+    """kunlun::CommonQ4Weight (k200.h:242-258): a device weight in the common layout."""
+
+    def __init__(self, device: int, k: int, n: int, storage=None, nbytes: int = 0):
+        self.handle = lib().k200_common_q4_weight_create(device, k, n, _ptr(storage), nbytes)
+
+    def upload(self, q4: np.ndarray) -> None:
+        src = np.ascontiguousarray(q4, np.uint8)
+        lib().k200_common_q4_weight_upload(self.handle, _ptr(src), src.nbytes)
+
+    def data(self) -> int:
+        return lib().k200_common_q4_weight_data(self.handle)
+
+    def info(self) -> dict:
+        a = _CommonQ4Info()
+        lib().k200_common_q4_weight_info(self.handle, C.byref(a))
+        return {name: getattr(a, name) for name, _ in _CommonQ4Info._fields_}
+
+    def close(self) -> None:
+        if self.handle:
+            lib().k200_common_q4_weight_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class CommonQ4Workspace:
+    """kunlun::CommonQ4Workspace (k200.h:279-303)."""
+
+    def __init__(self):
+        self.handle = lib().k200_common_q4_workspace_create()
+
+    def quantization(self) -> dict:
+        values, scales, out = C.c_void_p(), C.c_void_p(), (C.c_int * 3)()
+        lib().k200_common_q4_quantization(self.handle, C.byref(values), C.byref(scales), out)
+        return {"values": values.value, "scales": scales.value, "rows": out[0], "kp": out[1],
+                "components": out[2]}
+
+    def statistics(self) -> dict:
+        out = (C.c_size_t * 10)()
+        lib().k200_common_q4_statistics(self.handle, out)
+        return {"paths": list(out[:8]), "calls": out[8], "chunks": out[9]}
+
+    def close(self) -> None:
+        if self.handle:
+            lib().k200_common_q4_workspace_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def common_q4_matmul(workspace: CommonQ4Workspace, device: int, y, weight: CommonQ4Weight, x, m: int,
+                     type: int = INPUT_F32) -> None:
+    """Y [m,n] = X [m,k] . W^T; completes before returning (M=1: two-component A8, M>1: Row A8)."""
+    lib().k200_common_q4_matmul(workspace.handle, device, _ptr(y), weight.handle, _ptr(x), m, int(type))
 
 
 def matmul_count(device: int) -> int:

@@ -8,12 +8,11 @@
 #include "k200_internal.h"
 
 namespace k200 {
-cudaStream_t library_stream(int device);
 void set_stream(int device, cudaStream_t s);
 void set_static_weights(int device, bool on);
-const DeviceInfo &device_info(int device);
 int current_device();
 size_t matmul_count(int device);
+bool common_q4_pack(const void *raw, size_t bytes, int k, int n, void *out, size_t out_bytes);
 size_t peer_copy_count();
 size_t peer_byte_count();
 }  // namespace k200
@@ -116,6 +115,98 @@ int k200_matmul_i8_noalloc(int device, void *y, const void *w, const void *x, in
     static_assert(K200_NOALLOC_TOO_LARGE == k200::kNoAllocTooLarge, "k200_c.h status out of date");
     static_assert(K200_NOALLOC_NOT_READY == k200::kNoAllocNotReady, "k200_c.h status out of date");
     return k200::matmul_i8_noalloc(device, y, w, x, k, n, batch, scales, maxima);
+}
+
+// ---- native Q4 layout ---------------------------------------------------------
+int k200_native_q4_layout_supported(int k, int n) { return kunlun::native_q4_layout_supported(k, n) ? 1 : 0; }
+size_t k200_native_q4_size(int k, int n) { return kunlun::native_q4_size(k, n); }
+int k200_pack_native_q4(void *destination, size_t bytes, const void *q4, int k, int n) {
+    return kunlun::pack_native_q4(destination, bytes, q4, k, n) ? 1 : 0;
+}
+void k200_upload_native_q4(int device, void *weights, const void *q4, int k, int n) {
+    kunlun::upload_native_q4(device, weights, q4, k, n);
+}
+const char *k200_native_q4_reason(int k, int n, int batch, int type) {
+    kunlun::require(type == 0 || type == 1);
+    return kunlun::native_q4_reason(k, n, batch, static_cast<kunlun::InputType>(type));
+}
+void *k200_native_q4_workspace_create(void) { return new kunlun::NativeQ4Workspace(); }
+void k200_native_q4_workspace_destroy(void *workspace) { delete static_cast<kunlun::NativeQ4Workspace *>(workspace); }
+void k200_native_q4_statistics(void *workspace, size_t out[4]) {
+    kunlun::require(workspace && out);
+    const kunlun::NativeQ4Statistics s = static_cast<kunlun::NativeQ4Workspace *>(workspace)->statistics();
+    out[0] = s.accelerated;
+    out[1] = s.fallback;
+    out[2] = s.hbm_workspace_bytes;
+    out[3] = s.l3_workspace_bytes;
+}
+int k200_native_q4_matmul(void *workspace, int device, void *y, const void *weights, const void *input, int k, int n,
+                          int batch, int type) {
+    kunlun::require(workspace && (type == 0 || type == 1));
+    return kunlun::native_q4_matmul(*static_cast<kunlun::NativeQ4Workspace *>(workspace), device, y, weights, input, k,
+                                    n, batch, static_cast<kunlun::InputType>(type))
+               ? 1
+               : 0;
+}
+
+// ---- common Q4 ABI v1 ---------------------------------------------------------
+static_assert(sizeof(k200_common_q4_info) == sizeof(kunlun::CommonQ4Info), "k200_common_q4_info layout");
+int k200_common_q4_supported(int k, int n) { return kunlun::common_q4_supported(k, n) ? 1 : 0; }
+size_t k200_common_q4_size(int k, int n) { return kunlun::common_q4_size(k, n); }
+int k200_common_q4_pack(const void *q4, size_t bytes, int k, int n, void *out, size_t out_bytes) {
+    return k200::common_q4_pack(q4, bytes, k, n, out, out_bytes) ? 1 : 0;
+}
+void *k200_common_q4_weight_create(int device, int k, int n, void *storage, size_t bytes) {
+    return new kunlun::CommonQ4Weight(device, k, n, storage, bytes);
+}
+void k200_common_q4_weight_destroy(void *weight) { delete static_cast<kunlun::CommonQ4Weight *>(weight); }
+void k200_common_q4_weight_upload(void *weight, const void *q4, size_t bytes) {
+    kunlun::require(weight != nullptr);
+    static_cast<kunlun::CommonQ4Weight *>(weight)->upload(q4, bytes);
+}
+void *k200_common_q4_weight_data(void *weight) {
+    kunlun::require(weight != nullptr);
+    return static_cast<kunlun::CommonQ4Weight *>(weight)->data();
+}
+void k200_common_q4_weight_info(void *weight, k200_common_q4_info *out) {
+    kunlun::require(weight && out);
+    const kunlun::CommonQ4Info a = static_cast<kunlun::CommonQ4Weight *>(weight)->info();
+    out->abi_version = a.abi_version;
+    out->quant_type = a.quant_type;
+    out->layout = a.layout;
+    out->scale_order = a.scale_order;
+    out->k = a.k;
+    out->n = a.n;
+    out->kp = a.kp;
+    out->np = a.np;
+    out->device = a.device;
+    out->scale_offset = a.scale_offset;
+    out->payload_bytes = a.payload_bytes;
+}
+void *k200_common_q4_workspace_create(void) { return new kunlun::CommonQ4Workspace(); }
+void k200_common_q4_workspace_destroy(void *workspace) { delete static_cast<kunlun::CommonQ4Workspace *>(workspace); }
+void k200_common_q4_matmul(void *workspace, int device, void *y, const void *weight, const void *input, int m,
+                           int type) {
+    kunlun::require(workspace && weight && (type == 0 || type == 1));
+    kunlun::common_q4_matmul(*static_cast<kunlun::CommonQ4Workspace *>(workspace), device, y,
+                             *static_cast<const kunlun::CommonQ4Weight *>(weight), input, m,
+                             static_cast<kunlun::InputType>(type));
+}
+void k200_common_q4_quantization(void *workspace, const void **values, const void **scales, int out[3]) {
+    kunlun::require(workspace && values && scales && out);
+    const kunlun::CommonQ4Quantization q = static_cast<kunlun::CommonQ4Workspace *>(workspace)->quantization();
+    *values = q.values;
+    *scales = q.scales;
+    out[0] = q.rows;
+    out[1] = q.kp;
+    out[2] = q.components;
+}
+void k200_common_q4_statistics(void *workspace, size_t out[10]) {
+    kunlun::require(workspace && out);
+    const kunlun::CommonQ4Statistics s = static_cast<kunlun::CommonQ4Workspace *>(workspace)->statistics();
+    for (int i = 0; i < 8; ++i) out[i] = s.paths[i];
+    out[8] = s.calls;
+    out[9] = s.chunks;
 }
 
 }  // extern "C"

@@ -76,6 +76,33 @@ cudaError_t launch_elementwise(float *y, const float *a, const float *b, int n, 
 // GGML Q4_0 block quantiser (f32 [n][k] -> 18-byte blocks).
 cudaError_t launch_q4_0_quantize(const float *w, int n, int k, uint8_t *q4, cudaStream_t stream);
 
+// Native and common Q4 layouts (q4_layouts.cu).  dtype: 0 f32, 1 f16 input.
+// Two-component A8 of one activation vector, params {s0, s1, max0, max1}.
+// kq == 0: q0, q1 [k] int8; kq > 0 (the common layout's activation view):
+// element j at (j/32)*64 + j%32 of each [2*kq] component, the rest zero.
+cudaError_t launch_a8x2(const void *x, int k, int dtype, int kq, int8_t *q0, int8_t *q1, float *params,
+                        cudaStream_t stream);
+// Row A8 of m activation rows into [m][kq] int8 (zero past k), row scales
+// every scale_stride floats.
+cudaError_t launch_row_a8(const void *x, int m, int k, int dtype, int kq, int8_t *q, float *row_scale,
+                          int scale_stride, cudaStream_t stream);
+cudaError_t launch_native_gemv_a8x2(const uint8_t *w, const uint16_t *scales, const int8_t *q0, const int8_t *q1,
+                                    const float *params, int k, int n, float *y, const DeviceInfo &dev,
+                                    cudaStream_t stream);
+cudaError_t launch_native_fallback(const uint8_t *w, const uint16_t *scales, const void *x, int dtype, int k, int n,
+                                   int batch, float *y, const DeviceInfo &dev, cudaStream_t stream);
+cudaError_t launch_common_gemv_a8x2(const uint8_t *w, size_t scale_offset, int kp, int np, const int8_t *q0,
+                                    const int8_t *q1, const float *params, int k, int n, float *y,
+                                    const DeviceInfo &dev, cudaStream_t stream);
+// row_scale: one scale every 16 floats (the activation view's layout).
+cudaError_t launch_common_gemm_a8(const uint8_t *w, size_t scale_offset, int kp, int np, const int8_t *q,
+                                  const float *row_scale, int k, int n, int m, float *y, cudaStream_t stream);
+
+// Runtime hooks (runtime.cpp).
+cudaStream_t library_stream(int device);
+const DeviceInfo &device_info(int device);
+void count_matmul(int device);
+
 // Static scratch of the allocation-free rowwise-int8 matmul (static_scratch.cu):
 // room for batch*k <= kNoAllocMaxElements activations, two int8 components
 // each, plus a 256-byte parameter block.

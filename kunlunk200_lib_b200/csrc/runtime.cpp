@@ -456,6 +456,10 @@ size_t matmul_count(int device) {
     kunlun::require(device >= 0 && device < kunlun::kMaxDevices);
     return kunlun::devices[device].matmuls.load();
 }
+void count_matmul(int device) {
+    kunlun::require(device >= 0 && device < kunlun::kMaxDevices);
+    ++kunlun::devices[device].matmuls;
+}
 size_t peer_copy_count() { return kunlun::peer_copies.load(); }
 size_t peer_byte_count() { return kunlun::peer_bytes.load(); }
 

@@ -67,6 +67,23 @@ def test_cpp_api_symbols_match_reference_mangling(K):
         "_ZN6kunlun11elementwiseERNS_6KernelEiPvPKvS4_iiiNS_13ElementwiseOpEf",
         "_ZN6kunlun10statisticsEv",
         "_ZN6kunlun7versionEv",
+        # native and common Q4 layouts (k200.h:127-131, 203-335)
+        "_ZN6kunlun26native_q4_layout_supportedEii",
+        "_ZN6kunlun14native_q4_sizeEii",
+        "_ZN6kunlun14pack_native_q4EPvmPKvii",
+        "_ZN6kunlun16upload_native_q4EiPvPKvii",
+        "_ZN6kunlun16native_q4_reasonEiiiNS_9InputTypeE",
+        "_ZN6kunlun17NativeQ4WorkspaceC1Ev",
+        "_ZNK6kunlun17NativeQ4Workspace10statisticsEv",
+        "_ZN6kunlun16native_q4_matmulERNS_17NativeQ4WorkspaceEiPvPKvS4_iiiNS_9InputTypeE",
+        "_ZN6kunlun19common_q4_supportedEii",
+        "_ZN6kunlun14common_q4_sizeEii",
+        "_ZN6kunlun14CommonQ4WeightC1EiiiPvm",
+        "_ZN6kunlun14CommonQ4Weight6uploadEPKvm",
+        "_ZNK6kunlun14CommonQ4Weight4infoEv",
+        "_ZN6kunlun17CommonQ4WorkspaceC1Ev",
+        "_ZNK6kunlun17CommonQ4Workspace12quantizationEv",
+        "_ZN6kunlun16common_q4_matmulERNS_17CommonQ4WorkspaceEiPvRKNS_14CommonQ4WeightEPKviNS_9InputTypeE",
     ]
     missing = [s for s in expected if s not in exported]
     assert not missing, missing
@@ -81,7 +98,7 @@ def test_reference_consumers_link_against_this_library():
     """Reference programs compiled against the reference header resolve every
     symbol from this library (built by `make -C oracle consumers`)."""
     bindir = os.path.join(ROOT, "oracle", "_ref", "bin")
-    progs = [p for p in ("library-bench", "fused-bench", "native-q4-bench", "memory-example")
+    progs = [p for p in ("library-bench", "fused-bench", "native-q4-bench", "common-q4-bench", "memory-example")
              if os.path.exists(os.path.join(bindir, p))]
     if not progs:
         pytest.skip("reference consumer programs not built in this checkout")

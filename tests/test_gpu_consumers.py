@@ -58,3 +58,47 @@ def test_fused_bench(K, gpu):
 def test_memory_example(K, gpu):
     out = _run("memory-example")
     assert "PASS" in out
+
+
+# bench/native-q4-bench.cpp: mode PD K N batch dtype pattern trials.  The
+# program requires NMSE < 1e-5 (W4A8x2 path), < 1e-10 (exact fallback) or
+# < 1e-2 (cdnn) against its FP64 reference, and re-checks the native pack
+# byte by byte (its lines 40-47).
+NATIVE = [
+    ("native", 0, 4096, 4096, 1, "f32", 0, 3),
+    ("native", 0, 4096, 11008, 1, "f32", 1, 3),
+    ("native", 0, 11008, 4096, 1, "f16", 0, 3),
+    ("native", 0, 4096, 4096, 2, "f32", 0, 3),    # batch 2: exact fallback
+    ("native", 0, 1024, 1000, 1, "f16", 4, 3),    # N % 128 != 0: exact fallback
+    ("direct", 0, 4096, 4096, 1, "f32", 0, 3),
+    ("cdnn", 0, 4096, 4096, 1, "f32", 0, 3),
+]
+
+
+@pytest.mark.parametrize("args", NATIVE, ids=lambda a: "-".join(map(str, a)))
+def test_native_q4_bench(K, gpu, args):
+    out = _run("native-q4-bench", *args)
+    assert "RESULT mode=" + args[0] in out, out
+    expect_accelerated = args[0] == "native" and args[4] == 1 and args[3] % 128 == 0
+    if args[0] == "native":
+        assert f"accelerated={int(expect_accelerated)}" in out, out
+
+
+# bench/common-q4-bench.cpp: PD K N M dtype pattern trials common.  The
+# program requires implementation NMSE <= 1e-10 against the activations the
+# workspace's quantisation view reports, and checks the call and upload counts.
+COMMON = [
+    (0, 4096, 4096, 1, "f32", 0, 3, "common"),
+    (0, 4096, 11008, 1, "f16", 1, 3, "common"),
+    (0, 300, 1000, 1, "f32", 0, 3, "common"),      # K and N off the 256 padding
+    (0, 4096, 4096, 16, "f32", 0, 3, "common"),
+    (0, 2048, 3000, 128, "f16", 4, 3, "common"),
+    (0, 1024, 512, 300, "f32", 1, 3, "common"),    # three 128-row chunks
+]
+
+
+@pytest.mark.parametrize("args", COMMON, ids=lambda a: "-".join(map(str, a)))
+def test_common_q4_bench(K, gpu, args):
+    out = _run("common-q4-bench", *args)
+    assert '"correct":true' in out, out
+
