@@ -15,31 +15,26 @@
 // hi/lo truncation, about 2^-22 relative per term, plus f32 summation).
 //
 // Layout and work split:
-//  * the unit of work is a "pair": 32 rows x 144 bytes of the weight matrix
-//    (eight Q4_0 blocks of each row, two "groups" of four blocks).  Pairs
-//    are numbered row-tile-major and every CTA (one per SM) takes a
-//    contiguous range of them, so the bytes per CTA are balanced to within
-//    one pair;
-//  * a producer thread streams the CTA's range through a ring of stages with
-//    2-D TMA tensor copies (cp.async.bulk.tensor + mbarriers) of boxes of
-//    five or three pairs (32 rows x 720 or 432 bytes); each row tile's part
-//    of the range is cut into 5s and 3s, with 1-pair boxes only for
-//    segments of 1, 2, 4 or 7 pairs.  Measured on B200: boxes with 144-byte
-//    rows stream at ~2 TB/s, 432-1008-byte rows at 5.3-6.7 TB/s; the ring
-//    holds as many 23 KB stages as shared memory allows (6-8), since the
-//    bytes in flight per SM set the streaming rate.  Odd widths keep the
-//    shared-memory row pitch (36*w words) conflict-free for the lane pattern
-//    below;
-//  * consumer warp w processes pairs w, w + 16, ... of the range.  A stage
-//    holds one box; before waiting on a stage's mbarrier a warp checks the
-//    box sequence number the producer stored for the stage (a warp may run
-//    several boxes ahead, and an mbarrier parity alone only tells adjacent
-//    phases apart).  A stage's "empty" mbarrier counts five arrivals: one
-//    per pair from the warp that computed it, and the producer's for the
-//    pairs a narrower box lacks;
-//  * within a pair a warp computes two m16 tiles (rows 0-15 and 16-31) per
-//    group.  For group q the four blocks use the four column pairs of the
-//    n8 MMA: column pair i holds (hi, lo) of block beta(i)'s activations and
+//  * the unit of work is 16 rows x 144 bytes of the weight matrix (eight
+//    Q4_0 blocks of each row, two "groups" of four blocks).  Units are
+//    numbered row-tile-major and every CTA (one per SM) takes a contiguous
+//    range of them, so the bytes per CTA are balanced to within one unit;
+//  * a producer thread streams the CTA's range as "boxes" of 16 rows x 1-4
+//    units (2-D TMA tensor copies, cp.async.bulk.tensor + mbarriers): each
+//    row tile's part of the range is cut into boxes of four units (576-byte
+//    rows, read as 592 so that the row pitch in shared memory is bank-
+//    conflict-free) and one narrower box for the remainder;
+//  * the ring has 16 stages and box j lands in stage j mod 16.  Unit slot q
+//    of box j goes to consumer warp 4 (j mod 4) + q, so each stage is read by
+//    a fixed quad of warps, each warp meets a stage's phases in order, and
+//    the work per warp is balanced to within about one unit.  A warp
+//    computes its unit (one m16 tile per group of four blocks) and releases
+//    its slot with one mbarrier arrival (the producer arrives for the slots a
+//    narrow box lacks).  The producer records each box's position in a small
+//    table before its copy is issued, so the consumers need no box
+//    arithmetic;
+//  * within a group the four blocks use the four column pairs of the n8
+//    MMA: column pair i holds (hi, lo) of block beta(i)'s activations and
 //    zero elsewhere, so after the 8 MMAs of a group the accumulator holds
 //    four separate block dots and lane c of each quad finds block beta(c)
 //    in its own columns.  Each lane then applies d and the activation scale
@@ -48,13 +43,14 @@
 //    memory (544 bytes per group: the B fragments of the four column pairs,
 //    16 zero bytes and the four block scales), so the main loop reads them
 //    with one 16-byte load per block;
-//  * each warp leaves its partial sums of each row tile in shared memory;
-//    after the last pair the CTA's warps meet at one barrier and finish the
-//    CTA's tiles (one warp per tile): sum the warps' partials in warp order
-//    and store Y, or, for a tile shared with other CTAs, publish the sum (if
-//    a lower CTA holds the tile's first pairs) or collect the higher CTAs'
-//    published sums in CTA order before storing Y, so results do not depend
-//    on timing.
+//  * each warp keeps running row sums of its current row tile in registers
+//    and adds them to its own partial sums of that tile in shared memory when
+//    the tile changes; after the last box the CTA's warps meet at
+//    one barrier and finish the CTA's tiles (one warp per tile): sum the
+//    warps' partials in warp order and store Y, or, for a tile shared with
+//    other CTAs, publish the sum (if a lower CTA holds the tile's first
+//    units) or collect the higher CTAs' published sums in CTA order before
+//    storing Y, so results do not depend on timing.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -69,55 +65,42 @@ namespace k200 {
 
 namespace {
 
-constexpr int kTileRows = 32;
-constexpr int kPairBytes = 144;                        // two groups of four blocks
+constexpr int kTileRows = 16;                          // rows of a box: one m16 tile
+constexpr int kPairBytes = 144;                        // a unit's bytes per row: two groups of four blocks
 constexpr int kPairWords = kPairBytes / 4;
-constexpr int kMaxBoxPairs = 5;                        // widest box: 32 rows x 720 bytes
-constexpr int kStageBytes = kTileRows * kPairBytes * kMaxBoxPairs;  // 23040
-constexpr int kMinStages = 4, kMaxStages = 8;         // ring stages: as many as shared memory holds
+constexpr int kMaxBoxPairs = 4;                        // widest box: 16 rows x 4 units
+// Words a box row of w units occupies in shared memory: the units, plus four
+// words of the next bytes of the row when w is even, so that the row pitch
+// is 4 mod 8 words and the eight rows a load instruction touches (lane
+// pattern below) fall in different banks.
+__host__ __device__ constexpr int box_words(int w) { return kPairWords * w + ((w & 1) ? 0 : 4); }
+constexpr int kStageBytes = kTileRows * 4 * box_words(kMaxBoxPairs);  // 9472
 constexpr int kRecBytes = 544;                         // fragment record of one group
 constexpr int kZeroOff = 512, kScaleOff = 528;
 constexpr int kWarps = 16;                             // consumer warps
+constexpr int kStages = kWarps;                        // one ring stage per consumer warp
 constexpr int kThreads = (kWarps + 1) * 32;
 
 struct Q4MmaArgs {
     const float *x;
     float *y;
-    unsigned long long *slot;  // [grid][32] tagged partial sums of row tiles shared with other CTAs
+    unsigned long long *slot;  // [grid][16] tagged partial sums of row tiles shared with other CTAs
     int *err;
-    uint32_t units;     // row tiles * pairs per row (units * (grid + 1) < 2^32: 32-bit index math)
+    uint32_t units;     // row tiles * units per row (units * (grid + 1) < 2^32: 32-bit index math)
     int k, n, tiles, ppr, grid, prefetch;
     int max_tiles;      // row tiles any CTA touches (partial-sum slots in shared memory)
-    int stages;         // ring stages (kMinStages..kMaxStages)
+    int max_boxes;      // boxes any CTA streams (entries of the box table)
 };
 
 // Tensor maps over the weight rows viewed as 32-bit words [n][row_bytes/4],
-// with boxes of 32 rows x 5, 3 and 1 pairs.
+// with boxes of 16 rows x 1, 2, 3 and 4 units (box[w - 1] for width w).
 struct Q4MmaMaps {
-    CUtensorMap box[3];
+    CUtensorMap box[kMaxBoxPairs];
 };
-__host__ __device__ constexpr int map_of_width(int w) { return (kMaxBoxPairs - w) / 2; }
 
-// A segment of L pairs (a row tile's part of a CTA's range) is covered by
-// f5 five-pair boxes, then n3 three-pair boxes, then n1 one-pair boxes, with
-// 5*f5 + 3*n3 + n1 = L and n1 > 0 only for L = 1, 2, 4, 7.  The
-// decomposition of the remaining L - w after a first box of width w is the
-// rest of the decomposition of L, so a walk can pick each box from what is
-// left of the segment.
-struct Decomp {
-    int f5, n3, n1;
-};
-__host__ __device__ inline Decomp decomp(int L) {
-    const int f = L / 5, r = L - 5 * f;
-    if (r == 0) return {f, 0, 0};
-    if (r == 3) return {f, 1, 0};
-    if (r == 1) return f >= 1 ? Decomp{f - 1, 2, 0} : Decomp{0, 0, 1};
-    if (r == 4) return f >= 1 ? Decomp{f - 1, 3, 0} : Decomp{0, 1, 1};
-    return f >= 2 ? Decomp{f - 2, 4, 0} : f == 1 ? Decomp{0, 2, 1} : Decomp{0, 0, 2};  // r == 2
-}
-
-// The CTA's pairs [u, end) covered by boxes, segment by segment.  The
-// producer walks this sequence; consumers locate a pair in it with box_of().
+// The CTA's units [u, end) covered by boxes, segment by segment (a segment
+// is one row tile's part of the range): boxes of four units, then one box
+// for the rest of the segment.
 struct BoxWalk {
     int u, end;
     int tile, pair, width, ppr;
@@ -126,10 +109,7 @@ struct BoxWalk {
         pair = begin - tile * ppr;
         fit();
     }
-    __device__ void fit() {
-        const Decomp d = decomp(min(ppr - pair, end - u));
-        width = d.f5 ? 5 : d.n3 ? 3 : 1;
-    }
+    __device__ void fit() { width = min(kMaxBoxPairs, min(ppr - pair, end - u)); }
     __device__ void next() {
         u += width;
         pair += width;
@@ -138,38 +118,8 @@ struct BoxWalk {
     }
 };
 
-// Boxes that cover a segment of L pairs.
-__device__ __forceinline__ int boxes_in(int L) {
-    const Decomp d = decomp(L);
-    return d.f5 + d.n3 + d.n1;
-}
-
-// Position of a pair in the box sequence: segment [s0, s1) of its row tile
-// (pairs in row), its pair index p in the row, the boxes before the segment.
-struct BoxPos {
-    int box, q, width;  // box index in the CTA's sequence, pair within box, box width
-};
-__device__ __forceinline__ BoxPos box_of(int p, int s0, int s1, int before) {
-    const int o = p - s0;
-    const Decomp d = decomp(s1 - s0);
-    BoxPos b;
-    if (o < 5 * d.f5) {
-        b.box = o / 5;
-        b.q = o - 5 * b.box;
-        b.width = 5;
-    } else if (o < 5 * d.f5 + 3 * d.n3) {
-        const int o2 = o - 5 * d.f5, k3 = o2 / 3;
-        b.box = d.f5 + k3;
-        b.q = o2 - 3 * k3;
-        b.width = 3;
-    } else {
-        b.box = d.f5 + d.n3 + (o - 5 * d.f5 - 3 * d.n3);
-        b.q = 0;
-        b.width = 1;
-    }
-    b.box += before;
-    return b;
-}
+// Boxes that cover a segment of L units.
+__host__ __device__ constexpr int boxes_in(int L) { return (L + kMaxBoxPairs - 1) / kMaxBoxPairs; }
 
 // Column pair c of the MMA carries block beta(c) of a group, beta = (3, 1, 2, 0),
 // and lane c of a quad finishes that block; beta_inv is the inverse.
@@ -359,26 +309,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     q4_mma_gemv_kernel(const __grid_constant__ Q4MmaMaps maps, const Q4MmaArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int groups = a.k >> 7;
-    const int S = a.stages;
     uint8_t *ring = smem;
-    uint8_t *xrec = ring + S * kStageBytes;
-    float *part = reinterpret_cast<float *>(xrec + groups * kRecBytes);  // [max_tiles][kWarps][32]
-    uint64_t *full = reinterpret_cast<uint64_t *>(part + a.max_tiles * kWarps * 32);
-    uint64_t *empty = full + S;
-    volatile int *seqno = reinterpret_cast<volatile int *>(empty + S);  // box held by each stage
+    uint8_t *xrec = ring + kStages * kStageBytes;
+    float *part = reinterpret_cast<float *>(xrec + groups * kRecBytes);  // [max_tiles][kWarps][16]
+    uint64_t *full = reinterpret_cast<uint64_t *>(part + a.max_tiles * kWarps * kTileRows);
+    uint64_t *empty = full + kStages;
+    volatile uint32_t *box_tab = reinterpret_cast<volatile uint32_t *>(empty + kStages);  // [max_boxes]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int u0 = static_cast<int>(blockIdx.x * a.units / static_cast<uint32_t>(a.grid));
     const int u1 = static_cast<int>((blockIdx.x + 1) * a.units / static_cast<uint32_t>(a.grid));
-    const int nu = u1 - u0;
     const int t_first = u0 / a.ppr;
     const int t_last = (u1 - 1) / a.ppr;
 
-    if (tid < S) {
+    if (tid < kStages) {
         mbar_init(&full[tid], 1);
-        mbar_init(&empty[tid], kMaxBoxPairs);  // one arrival per pair slot of a box
+        mbar_init(&empty[tid], kMaxBoxPairs);  // one arrival per unit slot of a box
         fence_mbar_init();
-        seqno[tid] = -1;
     }
     __syncthreads();
     pdl_launch_dependents();
@@ -387,26 +334,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------- producer ----------------
         if (lane == 0) {
 #pragma unroll
-            for (int m = 0; m < 3; ++m)
+            for (int m = 0; m < kMaxBoxPairs; ++m)
                 asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.box[m])) : "memory");
             const uint64_t policy = policy_evict_first();
-            const int early = a.prefetch < S ? a.prefetch : S;
+            const int early = a.prefetch < kStages ? a.prefetch : kStages;
             const uint32_t ring_u = smem_u32(ring);
-            int j = 0, s = 0, phase = 0;
-            for (BoxWalk bw(u0, u1, a.ppr); bw.u < u1; bw.next(), ++j) {
-                if (j >= S && !mbar_wait(&empty[s], phase ^ 1, a.err, kErrBulkTimeout)) break;
+            int j = 0;
+            for (BoxWalk bw(u0, u1, a.ppr); bw.u < u1 && j < a.max_boxes; bw.next(), ++j) {
+                const int s = j % kStages;
+                if (j >= kStages && !mbar_wait(&empty[s], ((j / kStages) & 1) ^ 1, a.err, kErrBulkTimeout)) break;
                 if (j == early) pdl_wait_prior();
-                seqno[s] = j;
-                mbar_arrive_expect_tx(&full[s], kTileRows * kPairBytes * bw.width);
-                tma_load_2d(ring_u + s * kStageBytes, &maps.box[map_of_width(bw.width)], bw.pair * kPairWords,
+                // published to the consumer by the arrive below (release) and its wait (acquire)
+                box_tab[j] = static_cast<uint32_t>(bw.tile - t_first) | (static_cast<uint32_t>(bw.pair) << 16) |
+                             (static_cast<uint32_t>(bw.width) << 24);
+                mbar_arrive_expect_tx(&full[s], kTileRows * 4 * box_words(bw.width));
+                tma_load_2d(ring_u + s * kStageBytes, &maps.box[bw.width - 1], bw.pair * kPairWords,
                             bw.tile * kTileRows, &full[s], policy);
+                // the unit slots a narrow box lacks are released here
                 if (bw.width < kMaxBoxPairs) mbar_arrive_count(&empty[s], kMaxBoxPairs - bw.width);
-                if (++s == S) { s = 0; phase ^= 1; }
             }
             if (j <= early) pdl_wait_prior();
             // never exit with a copy still writing into this CTA's shared memory
-            for (int i = j > S ? j - S : 0; i < j; ++i)
-                (void)mbar_wait(&full[i % S], (i / S) & 1, a.err, kErrBulkTimeout);
+            for (int i = j > kStages ? j - kStages : 0; i < j; ++i)
+                (void)mbar_wait(&full[i % kStages], (i / kStages) & 1, a.err, kErrBulkTimeout);
         }
         return;
     }
@@ -432,7 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 store_slot(xv[k], xrec + (b >> 2) * kRecBytes, b & 3, lane & 3, t < nslots);
             }
     }
-    for (int i = tid; i < a.max_tiles * kWarps * 32; i += kWarps * 32) part[i] = 0.f;
+    for (int i = tid; i < a.max_tiles * kWarps * kTileRows; i += kWarps * 32) part[i] = 0.f;
     consumer_sync();
 
     const int g = lane >> 2, c = lane & 3;
@@ -452,23 +402,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int b = 0; b < 4; ++b) boff[b] = (g >> 1) == beta_inv(b) ? (g >> 1) * 128 + (g & 1) * 64 + c * 16 : kZeroOff;
 
-    // A row tile is finished by the last of this CTA's warps to arrive at it
-    // (every warp arrives once per tile of the CTA, with or without pairs in
-    // it).  The finishing warp sums the warps' partials in warp order, then
-    //  * stores Y if this CTA holds all of the tile's pairs;
-    //  * publishes the sum if a lower CTA holds the tile's first pairs (that
+    // A row tile is finished by one warp after every warp's partial sums are
+    // in shared memory.  The finishing warp (lanes 0-15, one row each) sums
+    // the warps' partials in warp order, then
+    //  * stores Y if this CTA holds all of the tile's units;
+    //  * publishes the sum if a lower CTA holds the tile's first units (that
     //    CTA finishes the tile; for this CTA it is always its first tile);
     //  * otherwise (the tile continues in higher CTAs) adds the sums those
     //    CTAs published, in CTA order, and stores Y.
     auto finish_tile = [&](int ts) {
+        if (lane >= kTileRows) return;
         const int t = t_first + ts;
         float v = 0.f;
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w) v += part[(ts * kWarps + w) * 32 + lane];
+        for (int w = 0; w < kWarps; ++w) v += part[(ts * kWarps + w) * kTileRows + lane];
         const int tb = t * a.ppr, te = tb + a.ppr;
         const int row = t * kTileRows + lane;
         if (tb < u0) {
-            st_relaxed(a.slot + static_cast<size_t>(blockIdx.x) * 32 + lane, kPresent | __float_as_uint(v));
+            st_relaxed(a.slot + static_cast<size_t>(blockIdx.x) * kTileRows + lane, kPresent | __float_as_uint(v));
             return;
         }
         if (te > u1) {
@@ -477,11 +428,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 unsigned long long wv[4];
 #pragma unroll
                 for (int q = 0; q < 4; ++q)
-                    wv[q] = j0 + q <= last ? ld_relaxed(a.slot + static_cast<size_t>(j0 + q) * 32 + lane) : kPresent;
+                    wv[q] = j0 + q <= last ? ld_relaxed(a.slot + static_cast<size_t>(j0 + q) * kTileRows + lane)
+                                           : kPresent;
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
                     if (j0 + q > last) break;
-                    unsigned long long *src = a.slot + static_cast<size_t>(j0 + q) * 32 + lane;
+                    unsigned long long *src = a.slot + static_cast<size_t>(j0 + q) * kTileRows + lane;
                     for (uint32_t spin = 0; !(wv[q] & kPresent); ++spin) {
                         if (spin >= kPeerBudget) {
                             atomicExch(a.err, kErrPeerTimeout);
@@ -498,107 +450,88 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (row < a.n) a.y[row] = v;
     };
 
-    const uint32_t ring_u = smem_u32(ring), xrec_u = smem_u32(xrec);
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};  // rows g, g+8, g+16, g+24 of the current tile
-    int cur = -1;
-    auto flush = [&](int t) {
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], 1);
-            acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], 2);
-        }
-        if (c == 0) {
-            float *dst = part + ((t - t_first) * kWarps + warp) * 32;
-#pragma unroll
-            for (int r = 0; r < 4; ++r) dst[g + 8 * r] = acc[r];
-        }
-#pragma unroll
-        for (int r = 0; r < 4; ++r) acc[r] = 0.f;
-    };
-
-    // this CTA's range in pair coordinates: first/last row tile, where the
-    // range starts in the first one and ends in the last one, and the boxes
-    // of the first segment and of a full row
+    // boxes of this CTA: the first segment, the full row tiles, the last segment
     const int p_first = u0 - t_first * a.ppr;
     const int p_end = u1 - t_last * a.ppr;
-    const int boxes_first = boxes_in((t_first == t_last ? p_end : a.ppr) - p_first);
-    const int boxes_row = boxes_in(a.ppr);
-    int tile = t_first, p = p_first + warp;
-    while (p >= a.ppr) { p -= a.ppr; ++tile; }
-    for (int i = warp; i < nu; i += kWarps) {
-        const int s0 = tile == t_first ? p_first : 0, s1 = tile == t_last ? p_end : a.ppr;
-        const int before = tile == t_first ? 0 : boxes_first + (tile - t_first - 1) * boxes_row;
-        const BoxPos bp = box_of(p, s0, s1, before);
-        const int j = bp.box, q = bp.q, width = bp.width;
-        const int s = j % S;
-        // wait until the stage holds box j, then for its bytes
-        if (seqno[s] != j) {
-            bool ok = true;
-            for (uint32_t spin = 0; seqno[s] != j; ++spin) {
-                if (spin >= kPeerBudget) { atomicExch(a.err, kErrBulkTimeout); ok = false; break; }
-                __nanosleep(32);
-            }
-            if (!ok) break;
+    const int nboxes = t_first == t_last ? boxes_in(p_end - p_first)
+                                         : boxes_in(a.ppr - p_first) + (t_last - t_first - 1) * boxes_in(a.ppr) +
+                                               boxes_in(p_end);
+    const uint32_t ring_u = smem_u32(ring), xrec_u = smem_u32(xrec);
+    // Warp 4r + q takes unit slot q of boxes r, r + 4, r + 8, ...: box j sits
+    // in stage j mod 16, so every stage is read by the same four warps and
+    // each warp meets a stage's phases in order.
+    const int quad_r = warp >> 2, slot_q = warp & 3;
+    float acc0 = 0.f, acc1 = 0.f;  // rows g and g + 8 of the current row tile
+    int cur = -1;
+    auto flush = [&](int t) {
+        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+        if (c == 0) {
+            float *dst = part + (t * kWarps + warp) * kTileRows;
+            dst[g] += acc0;
+            dst[g + 8] += acc1;
         }
-        if (!mbar_wait(&full[s], (j / S) & 1, a.err, kErrBulkTimeout)) break;
-        if (tile != cur) {
-            if (cur >= 0) flush(cur);
-            cur = tile;
-        }
-        const uint32_t pitch = kPairBytes * width;
-        // this lane's rows g, g+8, g+16, g+24 of the pair, at byte 4c of each group
-        const uint32_t r0 = ring_u + s * kStageBytes + q * kPairBytes + g * pitch + 4 * c;
-        const uint32_t rows[4] = {r0, r0 + 8 * pitch, r0 + 16 * pitch, r0 + 24 * pitch};
-        const uint32_t recp = xrec_u + p * 2 * kRecBytes;
-#pragma unroll
-        for (int grp = 0; grp < 2; ++grp) {
-            const uint32_t rec = recp + grp * kRecBytes;
-            uint32_t wq[4][4], dh[4];  // [row][block] nibble words, scale halves
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                const uint32_t ro = rows[r];
-                const uint32_t A = grp ? lds_at<72 + 4>(ro) : lds_at<4>(ro);
-                const uint32_t B = grp ? lds_at<72 + 20>(ro) : lds_at<20>(ro);
-                const uint32_t C = grp ? lds_at<72 + 36>(ro) : lds_at<36>(ro);
-                const uint32_t D = grp ? lds_at<72 + 56>(ro) : lds_at<56>(ro);
-                const uint32_t E = grp ? lds_at<72>(ro + offE) : lds_at<0>(ro + offE);
-                wq[r][0] = __byte_perm(A, E, selA);
-                wq[r][1] = B;
-                wq[r][2] = __byte_perm(C, E, selC);
-                wq[r][3] = D;
-                dh[r] = __byte_perm(E, E, selD);
+        acc0 = 0.f;
+        acc1 = 0.f;
+    };
+    for (int j = quad_r; j < nboxes && j < a.max_boxes; j += 4) {
+        const int s = j % kStages;
+        if (!mbar_wait(&full[s], (j / kStages) & 1, a.err, kErrBulkTimeout)) break;
+        const uint32_t info = box_tab[j];
+        const int width = static_cast<int>(info >> 24);
+        if (slot_q < width) {
+            const int tile_l = static_cast<int>(info & 0xffffu), pair = static_cast<int>((info >> 16) & 0xffu) + slot_q;
+            if (tile_l != cur) {
+                if (cur >= 0) flush(cur);
+                cur = tile_l;
             }
-            float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};  // tiles rows 0-15, 16-31
+            const uint32_t pitch = 4 * box_words(width);
+            // this lane's rows g and g+8 of the unit, at byte 4c of each group
+            const uint32_t ra = ring_u + s * kStageBytes + slot_q * kPairBytes + g * pitch + 4 * c;
+            const uint32_t rows[2] = {ra, ra + 8 * pitch};
+            const uint32_t recp = xrec_u + pair * 2 * kRecBytes;
 #pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                const uint4 xf = lds128(rec + boff[b]);
-                uint32_t t0[4], t1[4], t2[4], t3[4];
-                decode_word(wq[0][b], t0);
-                decode_word(wq[1][b], t1);
-                decode_word(wq[2][b], t2);
-                decode_word(wq[3][b], t3);
-                mma16816(d0, t0[0], t1[0], t0[1], t1[1], xf.x, xf.y);
-                mma16816(d1, t2[0], t3[0], t2[1], t3[1], xf.x, xf.y);
-                mma16816(d0, t0[2], t1[2], t0[3], t1[3], xf.z, xf.w);
-                mma16816(d1, t2[2], t3[2], t2[3], t3[3], xf.z, xf.w);
+            for (int grp = 0; grp < 2; ++grp) {
+                const uint32_t rec = recp + grp * kRecBytes;
+                uint32_t wq[2][4], dh[2];  // [row][block] nibble words, scale halves
+#pragma unroll
+                for (int r = 0; r < 2; ++r) {
+                    const uint32_t ro = rows[r];
+                    const uint32_t A = grp ? lds_at<72 + 4>(ro) : lds_at<4>(ro);
+                    const uint32_t B = grp ? lds_at<72 + 20>(ro) : lds_at<20>(ro);
+                    const uint32_t C = grp ? lds_at<72 + 36>(ro) : lds_at<36>(ro);
+                    const uint32_t D = grp ? lds_at<72 + 56>(ro) : lds_at<56>(ro);
+                    const uint32_t E = grp ? lds_at<72>(ro + offE) : lds_at<0>(ro + offE);
+                    wq[r][0] = __byte_perm(A, E, selA);
+                    wq[r][1] = B;
+                    wq[r][2] = __byte_perm(C, E, selC);
+                    wq[r][3] = D;
+                    dh[r] = __byte_perm(E, E, selD);
+                }
+                float d0[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const uint4 xf = lds128(rec + boff[b]);
+                    uint32_t t0[4], t1[4];
+                    decode_word(wq[0][b], t0);
+                    decode_word(wq[1][b], t1);
+                    mma16816(d0, t0[0], t1[0], t0[1], t1[1], xf.x, xf.y);
+                    mma16816(d0, t0[2], t1[2], t0[3], t1[3], xf.z, xf.w);
+                }
+                const float sig = ldsf(rec + kScaleOff + 4 * c);
+                const float s0 = __fmul_rn(half_bits_to_float(static_cast<uint16_t>(dh[0])), sig);
+                const float s1 = __fmul_rn(half_bits_to_float(static_cast<uint16_t>(dh[1])), sig);
+                acc0 = fmaf(s0, d0[0] + d0[1], acc0);
+                acc1 = fmaf(s1, d0[2] + d0[3], acc1);
             }
-            const float sig = ldsf(rec + kScaleOff + 4 * c);
-            const float s0 = __fmul_rn(half_bits_to_float(static_cast<uint16_t>(dh[0])), sig);
-            const float s1 = __fmul_rn(half_bits_to_float(static_cast<uint16_t>(dh[1])), sig);
-            const float s2 = __fmul_rn(half_bits_to_float(static_cast<uint16_t>(dh[2])), sig);
-            const float s3 = __fmul_rn(half_bits_to_float(static_cast<uint16_t>(dh[3])), sig);
-            acc[0] = fmaf(s0, d0[0] + d0[1], acc[0]);
-            acc[1] = fmaf(s1, d0[2] + d0[3], acc[1]);
-            acc[2] = fmaf(s2, d1[0] + d1[1], acc[2]);
-            acc[3] = fmaf(s3, d1[2] + d1[3], acc[3]);
+            // release this unit's slot of the stage; the proxy fence orders
+            // this warp's reads before the next TMA write into it
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
         }
-        // release this pair's slot of the stage; the proxy fence orders this
-        // warp's reads before the next TMA write into it
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-        p += kWarps;
-        while (p >= a.ppr) { p -= a.ppr; ++tile; }
     }
     if (cur >= 0) flush(cur);
     consumer_sync();  // every warp's partials are in shared memory
@@ -606,7 +539,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 struct Q4MmaPlan {
-    int grid, tiles, ppr, max_tiles, stages;
+    int grid, tiles, ppr, max_tiles, max_boxes;
     long long units;
     size_t smem;
 };
@@ -620,14 +553,11 @@ bool q4_mma_plan(Q4MmaPlan &p, int k, int n, const DeviceInfo &dev) {
     if (p.units * (p.grid + 1) >= (1ll << 32)) return false;  // the kernel's index math is 32-bit
     const long long per = (p.units + p.grid - 1) / p.grid;
     p.max_tiles = static_cast<int>((per + p.ppr - 1) / p.ppr + 1);
-    // each stage held by a consumer warp for ~a pair's compute time while the
-    // next boxes are in flight: the deeper the ring, the less the warps wait
-    for (p.stages = kMaxStages; p.stages >= kMinStages; --p.stages) {
-        p.smem = static_cast<size_t>(p.stages) * kStageBytes + static_cast<size_t>(k / 128) * kRecBytes +
-                 sizeof(float) * p.max_tiles * kWarps * 32 + 20 * p.stages + 16;
-        if (p.smem + 1024 <= static_cast<size_t>(dev.smem_optin)) return true;
-    }
-    return false;
+    p.max_boxes = static_cast<int>(per / kMaxBoxPairs + p.max_tiles + 1);  // >= the boxes of any range
+    if (p.tiles >= (1 << 16)) return false;                                 // box table: 16-bit tile index
+    p.smem = static_cast<size_t>(kStages) * kStageBytes + static_cast<size_t>(k / 128) * kRecBytes +
+             sizeof(float) * p.max_tiles * kWarps * kTileRows + 16 * kStages + 4 * static_cast<size_t>(p.max_boxes);
+    return p.smem + 1024 <= static_cast<size_t>(dev.smem_optin);
 }
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
@@ -669,9 +599,9 @@ bool weight_maps(Q4MmaMaps &out, const void *w, int k, int n) {
     cuuint64_t strides[1] = {row_bytes};
     cuuint32_t estr[2] = {1, 1};
     Q4MmaMaps maps;
-    for (int width = 1; width <= kMaxBoxPairs; width += 2) {
-        cuuint32_t box[2] = {static_cast<cuuint32_t>(kPairWords * width), kTileRows};
-        if (fn(&maps.box[map_of_width(width)], CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void *>(w), dims,
+    for (int width = 1; width <= kMaxBoxPairs; ++width) {
+        cuuint32_t box[2] = {static_cast<cuuint32_t>(box_words(width)), kTileRows};
+        if (fn(&maps.box[width - 1], CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void *>(w), dims,
                strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return false;
@@ -690,7 +620,7 @@ bool weight_maps(Q4MmaMaps &out, const void *w, int k, int n) {
 size_t q4_mma_scratch_bytes(int k, int n, int batch, const DeviceInfo &dev) {
     Q4MmaPlan p;
     if (batch != 1 || !q4_mma_plan(p, k, n, dev)) return 0;
-    return static_cast<size_t>(p.grid) * 32 * sizeof(unsigned long long);
+    return static_cast<size_t>(p.grid) * kTileRows * sizeof(unsigned long long);
 }
 
 cudaError_t launch_q4_mma_gemv(const GemvRequest &r, const DeviceInfo &dev, cudaStream_t stream) {
@@ -714,7 +644,7 @@ cudaError_t launch_q4_mma_gemv(const GemvRequest &r, const DeviceInfo &dev, cuda
     a.grid = p.grid;
     a.prefetch = r.prefetch_weights ? 1 << 30 : 0;
     a.max_tiles = p.max_tiles;
-    a.stages = p.stages;
+    a.max_boxes = p.max_boxes;
     static int configured[64] = {0};
     int devno = 0;
     cudaGetDevice(&devno);

@@ -94,13 +94,16 @@ def _q4_case(O, k, n, batch, seed=0x7340D123):
         (16384, 32, 1),      # one row tile split over many CTAs (cross-CTA sums)
         (16384, 100, 1),     # largest K, partial last tile
         (4352, 2049, 1),     # K/256 odd, N = 64*32 + 1
-        # tensor-core GEMV: row segments of every length class of the
-        # 5/3/1-pair box decomposition (K/256 = 2, 4, 7, 9, 12 pairs per row)
+        # tensor-core GEMV: row segments ending in every box width of the
+        # 4-unit box decomposition (K/256 = 2, 4, 7, 9, 12, 18 units per row:
+        # remainders 2, 0, 3, 1, 0, 2) and the largest K with many row tiles
         (512, 3000, 1),
         (1024, 777, 1),
         (1792, 2500, 1),
         (2304, 1500, 1),
         (3072, 4100, 1),
+        (4608, 1234, 1),
+        (16384, 5000, 1),
     ],
 )
 def test_q4_0_matches_fp64_gold(K, O, gpu, k, n, batch):
