@@ -162,6 +162,15 @@ void k200_common_q4_quantization(void *workspace, const void **values, const voi
 /* out = {paths[0..7], calls, chunks} */
 void k200_common_q4_statistics(void *workspace, size_t out[10]);
 
+/* Row gathers; 1 = rows written, 0 = contract violation or an index outside
+   [0, n) (no output written).  Replace kunlun::get_rows_f32
+   (src/get-rows-f32.inc:1-29) and kunlun::common_q4_get_rows
+   (src/get-rows.inc:1-26). */
+int k200_get_rows_f32(void *kernel, int device, void *output, size_t output_bytes, const void *input,
+                      size_t input_bytes, const int32_t *indices, size_t index_bytes, int k, int n, int rows);
+int k200_common_q4_get_rows(void *kernel, int device, void *output, size_t output_bytes, void *weight,
+                            const int32_t *indices, size_t index_bytes, int rows);
+
 #ifdef __cplusplus
 }
 #endif

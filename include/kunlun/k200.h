@@ -79,6 +79,8 @@ enum class InputType { f32, f16 };
 
 // Per-call state: device binding and lazily grown scratch (quantised
 // activations of the rowwise int8 path).  Bound to the first device used.
+class CommonQ4Weight;
+
 class Kernel {
 public:
     Kernel();
@@ -92,6 +94,10 @@ private:
                        const float *, int);
     friend void elementwise(Kernel &, int, void *, const void *, const void *, int, int, int, ElementwiseOp,
                             float);
+    friend bool get_rows_f32(Kernel &, int, void *, size_t, const void *, size_t, const int32_t *, size_t, int, int,
+                             int);
+    friend bool common_q4_get_rows(Kernel &, int, void *, size_t, const CommonQ4Weight &, const int32_t *, size_t,
+                                   int);
 };
 
 // Rowwise int8 weights: aligned(k*rows) int8 values, then aligned(rows*4)
@@ -220,6 +226,16 @@ private:
 // M > 1: one int8 scale per activation row (Row A8).
 void common_q4_matmul(CommonQ4Workspace &, int device, void *y, const CommonQ4Weight &, const void *input, int m,
                       InputType type = InputType::f32);
+
+// Row gathers: output[r] = input row indices[r] (F32 rows; K % 16 == 0,
+// 16 <= K <= 1048576) or the decoded common-Q4 weight column indices[r]
+// (K % 64 == 0), rows = 1..512, output 64-byte aligned.  Complete before
+// returning; false (and no output written) on a contract violation or an
+// index outside [0, n).
+bool get_rows_f32(Kernel &, int device, void *output, size_t output_bytes, const void *input, size_t input_bytes,
+                  const int32_t *indices, size_t index_bytes, int k, int n, int rows);
+bool common_q4_get_rows(Kernel &, int device, void *output, size_t output_bytes, const CommonQ4Weight &,
+                        const int32_t *indices, size_t index_bytes, int rows);
 
 struct Statistics {
     size_t matmuls[2];            // devices 0 and 1 (ABI of the reference struct)

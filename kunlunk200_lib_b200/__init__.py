@@ -90,6 +90,10 @@ _SIGNATURES = {
     "k200_common_q4_quantization": (None, [C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
                                            C.POINTER(C.c_int)]),
     "k200_common_q4_statistics": (None, [C.c_void_p, C.POINTER(C.c_size_t)]),
+    "k200_get_rows_f32": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_void_p,
+                                    C.c_size_t, C.c_int, C.c_int, C.c_int]),
+    "k200_common_q4_get_rows": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p,
+                                          C.c_size_t, C.c_int]),
 }
 
 # kunlun::InputType values (k200.h:132)
@@ -482,6 +486,20 @@ def common_q4_matmul(workspace: CommonQ4Workspace, device: int, y, weight: Commo
                      type: int = INPUT_F32) -> None:
     """Y [m,n] = X [m,k] . W^T; completes before returning (M=1: two-component A8, M>1: Row A8)."""
     lib().k200_common_q4_matmul(workspace.handle, device, _ptr(y), weight.handle, _ptr(x), m, int(type))
+
+
+def get_rows_f32(kernel: Kernel, device: int, output, output_bytes: int, input, input_bytes: int, indices,
+                 index_bytes: int, k: int, n: int, rows: int) -> bool:
+    """kunlun::get_rows_f32 (src/get-rows-f32.inc:1-29): completes before returning; False writes nothing."""
+    return bool(lib().k200_get_rows_f32(kernel.handle, device, _ptr(output), output_bytes, _ptr(input), input_bytes,
+                                        _ptr(indices), index_bytes, k, n, rows))
+
+
+def common_q4_get_rows(kernel: Kernel, device: int, output, output_bytes: int, weight: CommonQ4Weight, indices,
+                       index_bytes: int, rows: int) -> bool:
+    """kunlun::common_q4_get_rows (src/get-rows.inc:1-26): decoded F32 weight columns by index."""
+    return bool(lib().k200_common_q4_get_rows(kernel.handle, device, _ptr(output), output_bytes, weight.handle,
+                                              _ptr(indices), index_bytes, rows))
 
 
 def matmul_count(device: int) -> int:

@@ -209,4 +209,20 @@ void k200_common_q4_statistics(void *workspace, size_t out[10]) {
     out[9] = s.chunks;
 }
 
+int k200_get_rows_f32(void *kernel, int device, void *output, size_t output_bytes, const void *input,
+                      size_t input_bytes, const int32_t *indices, size_t index_bytes, int k, int n, int rows) {
+    return kunlun::get_rows_f32(*static_cast<kunlun::Kernel *>(kernel), device, output, output_bytes, input,
+                                input_bytes, indices, index_bytes, k, n, rows)
+               ? 1
+               : 0;
+}
+
+int k200_common_q4_get_rows(void *kernel, int device, void *output, size_t output_bytes, void *weight,
+                            const int32_t *indices, size_t index_bytes, int rows) {
+    return kunlun::common_q4_get_rows(*static_cast<kunlun::Kernel *>(kernel), device, output, output_bytes,
+                                      *static_cast<kunlun::CommonQ4Weight *>(weight), indices, index_bytes, rows)
+               ? 1
+               : 0;
+}
+
 }  // extern "C"

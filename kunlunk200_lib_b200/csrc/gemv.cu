@@ -770,6 +770,7 @@ cudaError_t launch_gemv(const GemvRequest &r, const DeviceInfo &dev, cudaStream_
         const cudaError_t e = launch_q4_mma_gemv(r, dev, stream);
         if (e != cudaErrorNotSupported) return e;
     }
+    if (r.wt == 0 && gemm_f32_supported(r)) return launch_gemm_f32(r, dev, stream);
     const long long row_bytes = r.wt == 0 ? 4ll * r.k : r.wt == 1 ? 2ll * r.k : r.wt == 2 ? 18ll * (r.k / 32) : r.k;
     const bool fast = gemv_fast_path_ok(r.wt, r.w, r.x, r.y, r.k, row_bytes);
     for (int c0 = 0; c0 < r.batch; c0 += 2) {

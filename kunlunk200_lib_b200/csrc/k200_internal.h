@@ -55,6 +55,20 @@ bool gemm_tc_supported(int wt, int k, int n, int batch);  // (q4_0 also needs k 
 size_t gemm_tc_scratch_bytes(int wt, int k, int n, int batch);
 cudaError_t launch_gemm_tc(const GemvRequest &r, const DeviceInfo &dev, cudaStream_t stream);
 cudaError_t launch_q4_mma_gemv(const GemvRequest &r, const DeviceInfo &dev, cudaStream_t stream);
+// Row gathers (get_rows.cu); an index outside [0, n) writes no output and
+// sets *status to 1 (else 0).
+cudaError_t launch_get_rows_f32(float *out, const float *in, const int32_t *idx, int *status, int k, int n, int rows,
+                                cudaStream_t stream);
+cudaError_t launch_common_get_rows(float *out, const uint8_t *w, size_t scale_offset, int kp, int np,
+                                   const int32_t *idx, int *status, int k, int n, int rows, cudaStream_t stream);
+// FP32 SIMT GEMM for f32 weights at batch >= kF32GemmMinBatch and K % 64 == 0
+// (gemm_f32.cu): reads W once per tile of up to 64 columns instead of once
+// per column pair.  Measured on B200 at K = N = 8192 it streams the weights
+// at ~1.5 TB/s, so below 9 columns the column-pair streaming kernel (one
+// ~6 TB/s pass per two columns) is faster.
+constexpr int kF32GemmMinBatch = 9;
+bool gemm_f32_supported(const GemvRequest &r);
+cudaError_t launch_gemm_f32(const GemvRequest &r, const DeviceInfo &dev, cudaStream_t stream);
 bool gemv_fast_path_ok(int wt, const void *w, const void *x, const void *y, int k, long long row_bytes);
 
 // Per-tensor two-component A8 quantiser of the rowwise-int8 path

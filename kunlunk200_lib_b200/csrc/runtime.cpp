@@ -262,6 +262,7 @@ struct Kernel::Impl {
     size_t fixup_size = 0;
     void *split = nullptr;   // tensor-core GEMM: activations split into f16 hi/lo
     size_t split_size = 0;
+    void *rows_status = nullptr;  // row gathers: index verdict written by the kernel (256 bytes)
 };
 
 Kernel::Kernel() : impl_(new Impl{}) {}
@@ -276,6 +277,7 @@ Kernel::~Kernel() {
         release(s.id, s.alias, s.alias_size);
         release(s.id, s.fixup, s.fixup_size);
         release(s.id, s.split, s.split_size);
+        release(s.id, s.rows_status, 256);
     }
     delete impl_;
 }
@@ -417,6 +419,81 @@ void elementwise(Kernel &kernel, int id, void *y, const void *a, const void *b, 
                                         static_cast<const float *>(b), n, width, bn, op, parameter, d.info,
                                         d.stream));
     check(wait());
+}
+
+// ---------------------------------------------------------------------------
+// row gathers (src/get-rows-f32.inc, src/get-rows.inc)
+// ---------------------------------------------------------------------------
+namespace {
+bool spans_overlap(const void *a, size_t an, const void *b, size_t bn) {
+    const uintptr_t x = (uintptr_t)a, y = (uintptr_t)b;
+    return x < y + bn && y < x + an;
+}
+bool fits(const void *p, size_t bytes) { return (uintptr_t)p <= UINTPTR_MAX - bytes; }
+
+// Binds the Kernel to `id` and returns its status word (allocated on first use).
+int *rows_status(Kernel::Impl &s, int id) {
+    require(s.id < 0 || s.id == id);
+    s.id = id;
+    select(id);
+    if (!s.rows_status) {
+        s.rows_status = allocate(id, 256);
+        require(s.rows_status != nullptr);
+    }
+    return static_cast<int *>(s.rows_status);
+}
+
+// Completes the gather and reads the kernel's verdict (0: every index valid).
+bool rows_verdict(const int *status) {
+    int verdict = 1;
+    check(copy(&verdict, status, sizeof(verdict), device_to_host));
+    return verdict == 0;
+}
+}  // namespace
+
+bool get_rows_f32(Kernel &kernel, int id, void *output, size_t output_bytes, const void *input, size_t input_bytes,
+                  const int32_t *indices, size_t index_bytes, int k, int n, int rows) {
+    std::lock_guard<std::recursive_mutex> lock(mutex);
+    if (id < 0 || id >= cuda_device_count() || k < 16 || k > 1048576 || k % 16 || n < 1 || rows < 1 || rows > 512)
+        return false;
+    const size_t row_bytes = (size_t)k * 4;
+    if ((size_t)n > SIZE_MAX / row_bytes) return false;
+    const size_t xbytes = (size_t)n * row_bytes, ybytes = (size_t)rows * row_bytes, ibytes = (size_t)rows * 4;
+    if (!output || !input || !indices || (uintptr_t)output % 64 || (uintptr_t)input % 64 || (uintptr_t)indices % 4 ||
+        output_bytes < ybytes || input_bytes < xbytes || index_bytes < ibytes)
+        return false;
+    if (!fits(output, ybytes) || !fits(input, xbytes) || !fits(indices, ibytes)) return false;
+    if (spans_overlap(output, ybytes, input, xbytes) || spans_overlap(output, ybytes, indices, ibytes) ||
+        spans_overlap(input, xbytes, indices, ibytes))
+        return false;
+    int *status = rows_status(*kernel.impl_, id);
+    DeviceState &d = state(id);
+    check((int)k200::launch_get_rows_f32(static_cast<float *>(output), static_cast<const float *>(input), indices,
+                                         status, k, n, rows, d.stream));
+    return rows_verdict(status);
+}
+
+bool common_q4_get_rows(Kernel &kernel, int id, void *output, size_t output_bytes, const CommonQ4Weight &weight,
+                        const int32_t *indices, size_t index_bytes, int rows) {
+    std::lock_guard<std::recursive_mutex> lock(mutex);
+    const CommonQ4Info a = weight.info();
+    if (a.abi_version != 1 || a.quant_type != 2 || a.layout != 1 || a.scale_order != 1 ||
+        weight.statistics().uploads == 0 || a.device != id || id < 0 || id >= cuda_device_count() || a.k % 64 ||
+        rows < 1 || rows > 512)
+        return false;
+    const size_t ybytes = (size_t)rows * a.k * 4, ibytes = (size_t)rows * 4;
+    if (!output || !indices || (uintptr_t)output % 64 || (uintptr_t)indices % 4 || output_bytes < ybytes ||
+        index_bytes < ibytes)
+        return false;
+    require(fits(output, ybytes) && fits(indices, ibytes) && fits(weight.data(), a.payload_bytes));
+    if (spans_overlap(output, ybytes, indices, ibytes) || spans_overlap(output, ybytes, weight.data(), a.payload_bytes) ||
+        spans_overlap(indices, ibytes, weight.data(), a.payload_bytes))
+        return false;
+    int *status = rows_status(*kernel.impl_, id);
+    DeviceState &d = state(id);
+    check((int)k200::launch_common_get_rows(static_cast<float *>(output), static_cast<const uint8_t *>(weight.data()),
+                                            a.scale_offset, a.kp, a.np, indices, status, a.k, a.n, rows, d.stream));
+    return rows_verdict(status);
 }
 
 Statistics statistics() {

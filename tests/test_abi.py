@@ -84,6 +84,9 @@ def test_cpp_api_symbols_match_reference_mangling(K):
         "_ZN6kunlun17CommonQ4WorkspaceC1Ev",
         "_ZNK6kunlun17CommonQ4Workspace12quantizationEv",
         "_ZN6kunlun16common_q4_matmulERNS_17CommonQ4WorkspaceEiPvRKNS_14CommonQ4WeightEPKviNS_9InputTypeE",
+        # row gathers (k200.h:339-343)
+        "_ZN6kunlun12get_rows_f32ERNS_6KernelEiPvmPKvmPKimiii",
+        "_ZN6kunlun18common_q4_get_rowsERNS_6KernelEiPvmRKNS_14CommonQ4WeightEPKimi",
     ]
     missing = [s for s in expected if s not in exported]
     assert not missing, missing
@@ -98,7 +101,8 @@ def test_reference_consumers_link_against_this_library():
     """Reference programs compiled against the reference header resolve every
     symbol from this library (built by `make -C oracle consumers`)."""
     bindir = os.path.join(ROOT, "oracle", "_ref", "bin")
-    progs = [p for p in ("library-bench", "fused-bench", "native-q4-bench", "common-q4-bench", "memory-example")
+    progs = [p for p in ("library-bench", "fused-bench", "native-q4-bench", "common-q4-bench", "get-rows-test",
+                         "get-rows-f32-test", "memory-example")
              if os.path.exists(os.path.join(bindir, p))]
     if not progs:
         pytest.skip("reference consumer programs not built in this checkout")

@@ -102,3 +102,24 @@ def test_common_q4_bench(K, gpu, args):
     out = _run("common-q4-bench", *args)
     assert '"correct":true' in out, out
 
+
+# bench/get-rows-f32-test.cpp: PD.  Bitwise row copies for K in {16, 80, 2048,
+# 4096} and M in {1, 3, 128, 512}, guard words around the output, indices -1 and
+# N rejected without a write, and short buffers rejected.
+def test_get_rows_f32_test(K, gpu):
+    out = _run("get-rows-f32-test", 0)
+    assert "F32_ROWS" in out and "bitwise=1" in out, out
+
+
+# bench/get-rows-test.cpp: FILE OFFSET K N PD TIMING.  Decodes common-Q4 weight
+# columns by index and compares them bit for bit with its own Q4_0 decode of
+# the raw blocks read from FILE at OFFSET; invalid indices must write nothing.
+@pytest.mark.parametrize("k,n", [(4096, 1000), (256, 33)])
+def test_get_rows_test(K, O, gpu, tmp_path, k, n):
+    raw = O.fixture_q4(k, n)
+    path = tmp_path / "weights.q4"
+    path.write_bytes(b"\0" * 96 + raw.tobytes())
+    out = _run("get-rows-test", str(path), 96, k, n, 0, 0)
+    assert "GET_ROWS_UNIT_PASS invalid_ids_rejected=1" in out, out
+    assert out.count("bitwise=1") == 4, out
+

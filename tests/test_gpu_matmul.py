@@ -206,6 +206,19 @@ def test_dense_matches_fp64_gold(K, O, gpu, wtype, k, n, batch):
         _check_float(y, gold)
 
 
+@pytest.mark.parametrize("k,n,batch", [(8192, 1000, 64), (4096, 300, 17), (1024, 129, 33), (64, 70, 100),
+                                       (8192, 8193, 9), (8192, 8193, 4), (96, 40, 12)])
+def test_f32_batched_gemm(K, O, gpu, k, n, batch):
+    """f32 weights at batch >= 9 and K % 64 == 0 (the FP32 SIMT GEMM: 32-term FP32
+    FMA chains added in double), and the streaming kernel at the other shapes,
+    held to the F32 bar of the FP32 path."""
+    w = O.uniform(0x7340D123, n * k, -1.0, 1.0)
+    x = O.uniform(0x09200ABC, k * batch, -1.0, 1.0)
+    gold = O.matmul_gold(w, O.WT_F32, x, k, n, batch)
+    y = _device_matmul(K, K.F32, w, x, k, n, batch)
+    _check_float(y, gold)
+
+
 @pytest.mark.parametrize("wtype", ["f16", "f32"])
 def test_dense_library_bench_closed_form(K, O, gpu, wtype):
     """bench/library-bench.cpp:89-101: its f32 weights are exact in f16, so both
