@@ -171,6 +171,15 @@ int k200_get_rows_f32(void *kernel, int device, void *output, size_t output_byte
 int k200_common_q4_get_rows(void *kernel, int device, void *output, size_t output_bytes, void *weight,
                             const int32_t *indices, size_t index_bytes, int rows);
 
+/* Fused SiLU(gate) * up over rows at byte strides; type 0 = f32, 1 = f16.
+   Replace kunlun::swiglu_reason / kunlun::swiglu (src/k200.cpp:324-368);
+   k200_swiglu returns 1 when done, 0 for an unsupported layout or pointer
+   contract (nothing submitted). */
+const char *k200_swiglu_reason(int width, int rows, int gate_stride, int up_stride, int output_stride, int type);
+int k200_swiglu(void *kernel, int device, void *y, size_t y_bytes, const void *gate, size_t gate_bytes,
+                const void *up, size_t up_bytes, int width, int rows, int gate_stride, int up_stride,
+                int output_stride, int type);
+
 #ifdef __cplusplus
 }
 #endif

@@ -80,6 +80,7 @@ enum class InputType { f32, f16 };
 // Per-call state: device binding and lazily grown scratch (quantised
 // activations of the rowwise int8 path).  Bound to the first device used.
 class CommonQ4Weight;
+struct SwiGLULayout;
 
 class Kernel {
 public:
@@ -98,6 +99,8 @@ private:
                              int);
     friend bool common_q4_get_rows(Kernel &, int, void *, size_t, const CommonQ4Weight &, const int32_t *, size_t,
                                    int);
+    friend bool swiglu(Kernel &, int, void *, size_t, const void *, size_t, const void *, size_t,
+                       const SwiGLULayout &);
 };
 
 // Rowwise int8 weights: aligned(k*rows) int8 values, then aligned(rows*4)
@@ -236,6 +239,20 @@ bool get_rows_f32(Kernel &, int device, void *output, size_t output_bytes, const
                   const int32_t *indices, size_t index_bytes, int k, int n, int rows);
 bool common_q4_get_rows(Kernel &, int device, void *output, size_t output_bytes, const CommonQ4Weight &,
                         const int32_t *indices, size_t index_bytes, int rows);
+
+// Fused gate/up activation: y = SiLU(gate) * up with F32 intermediates and
+// one final rounding, rows of `width` contiguous F32 or F16 values at byte
+// strides.  An empty reason means supported.  Completes before returning;
+// false means an unsupported layout or pointer contract (nothing submitted).
+// An exact alias of y with gate or up (same start and row stride) is allowed.
+struct SwiGLULayout {
+    int width, rows;
+    int gate_stride, up_stride, output_stride;  // bytes between rows
+    InputType type;
+};
+const char *swiglu_reason(const SwiGLULayout &);
+bool swiglu(Kernel &, int device, void *y, size_t y_bytes, const void *gate, size_t gate_bytes, const void *up,
+            size_t up_bytes, const SwiGLULayout &);
 
 struct Statistics {
     size_t matmuls[2];            // devices 0 and 1 (ABI of the reference struct)

@@ -94,6 +94,9 @@ _SIGNATURES = {
                                     C.c_size_t, C.c_int, C.c_int, C.c_int]),
     "k200_common_q4_get_rows": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p,
                                           C.c_size_t, C.c_int]),
+    "k200_swiglu_reason": (C.c_char_p, [C.c_int] * 6),
+    "k200_swiglu": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_void_p,
+                              C.c_size_t] + [C.c_int] * 6),
 }
 
 # kunlun::InputType values (k200.h:132)
@@ -500,6 +503,19 @@ def common_q4_get_rows(kernel: Kernel, device: int, output, output_bytes: int, w
     """kunlun::common_q4_get_rows (src/get-rows.inc:1-26): decoded F32 weight columns by index."""
     return bool(lib().k200_common_q4_get_rows(kernel.handle, device, _ptr(output), output_bytes, weight.handle,
                                               _ptr(indices), index_bytes, rows))
+
+
+def swiglu_reason(width: int, rows: int, gate_stride: int, up_stride: int, output_stride: int,
+                  type: int = INPUT_F32) -> str:
+    """kunlun::swiglu_reason (src/k200.cpp:324-333): "" when the layout is supported."""
+    return lib().k200_swiglu_reason(width, rows, gate_stride, up_stride, output_stride, int(type)).decode()
+
+
+def swiglu(kernel: Kernel, device: int, y, y_bytes: int, gate, gate_bytes: int, up, up_bytes: int, width: int,
+           rows: int, gate_stride: int, up_stride: int, output_stride: int, type: int = INPUT_F32) -> bool:
+    """kunlun::swiglu (src/k200.cpp:334-368): y = SiLU(gate) * up; completes before returning."""
+    return bool(lib().k200_swiglu(kernel.handle, device, _ptr(y), y_bytes, _ptr(gate), gate_bytes, _ptr(up), up_bytes,
+                                  width, rows, gate_stride, up_stride, output_stride, int(type)))
 
 
 def matmul_count(device: int) -> int:

@@ -217,6 +217,23 @@ int k200_get_rows_f32(void *kernel, int device, void *output, size_t output_byte
                : 0;
 }
 
+const char *k200_swiglu_reason(int width, int rows, int gate_stride, int up_stride, int output_stride, int type) {
+    const kunlun::SwiGLULayout p{width, rows, gate_stride, up_stride, output_stride,
+                                 static_cast<kunlun::InputType>(type)};
+    return kunlun::swiglu_reason(p);
+}
+
+int k200_swiglu(void *kernel, int device, void *y, size_t y_bytes, const void *gate, size_t gate_bytes,
+                const void *up, size_t up_bytes, int width, int rows, int gate_stride, int up_stride,
+                int output_stride, int type) {
+    const kunlun::SwiGLULayout p{width, rows, gate_stride, up_stride, output_stride,
+                                 static_cast<kunlun::InputType>(type)};
+    return kunlun::swiglu(*static_cast<kunlun::Kernel *>(kernel), device, y, y_bytes, gate, gate_bytes, up,
+                          up_bytes, p)
+               ? 1
+               : 0;
+}
+
 int k200_common_q4_get_rows(void *kernel, int device, void *output, size_t output_bytes, void *weight,
                             const int32_t *indices, size_t index_bytes, int rows) {
     return kunlun::common_q4_get_rows(*static_cast<kunlun::Kernel *>(kernel), device, output, output_bytes,

@@ -61,6 +61,9 @@ cudaError_t launch_get_rows_f32(float *out, const float *in, const int32_t *idx,
                                 cudaStream_t stream);
 cudaError_t launch_common_get_rows(float *out, const uint8_t *w, size_t scale_offset, int kp, int np,
                                    const int32_t *idx, int *status, int k, int n, int rows, cudaStream_t stream);
+// kunlun::swiglu (swiglu.cu): y = SiLU(gate) * up, strides in bytes, f16 != 0: F16 rows.
+cudaError_t launch_swiglu(void *y, const void *gate, const void *up, int width, int rows, int gs, int us, int ys,
+                          int f16, const DeviceInfo &dev, cudaStream_t stream);
 // FP32 SIMT GEMM for f32 weights at batch >= kF32GemmMinBatch and K % 64 == 0
 // (gemm_f32.cu): reads W once per tile of up to 64 columns instead of once
 // per column pair.  Measured on B200 at K = N = 8192 it streams the weights

@@ -496,6 +496,54 @@ bool common_q4_get_rows(Kernel &kernel, int id, void *output, size_t output_byte
     return rows_verdict(status);
 }
 
+// ---------------------------------------------------------------------------
+// swiglu (src/k200.cpp:324-368)
+// ---------------------------------------------------------------------------
+const char *swiglu_reason(const SwiGLULayout &p) {
+    if (p.type != InputType::f32 && p.type != InputType::f16) return "type";
+    const int bytes = p.type == InputType::f32 ? 4 : 2;
+    if (p.width <= 0 || p.width > 65536 || p.rows <= 0 || p.rows > INT_MAX / p.width / bytes) return "shape";
+    for (int stride : {p.gate_stride, p.up_stride, p.output_stride}) {
+        if (stride < p.width * bytes || stride % bytes) return "stride";
+        if ((size_t)(p.rows - 1) * stride + (size_t)p.width * bytes > INT_MAX) return "byte extent";
+    }
+    return "";
+}
+
+bool swiglu(Kernel &kernel, int id, void *y, size_t y_bytes, const void *gate, size_t gate_bytes, const void *up,
+            size_t up_bytes, const SwiGLULayout &p) {
+    std::lock_guard<std::recursive_mutex> lock(mutex);
+    if (*swiglu_reason(p) || id < 0 || id >= cuda_device_count() || !y || !gate || !up) return false;
+    const int bytes = p.type == InputType::f32 ? 4 : 2;
+    const uintptr_t yp = (uintptr_t)y, gp = (uintptr_t)gate, upp = (uintptr_t)up;
+    const size_t ys = (size_t)(p.rows - 1) * p.output_stride + (size_t)p.width * bytes;
+    const size_t gs = (size_t)(p.rows - 1) * p.gate_stride + (size_t)p.width * bytes;
+    const size_t us = (size_t)(p.rows - 1) * p.up_stride + (size_t)p.width * bytes;
+    if (ys > y_bytes || gs > gate_bytes || us > up_bytes || yp % bytes || gp % bytes || upp % bytes) return false;
+    if (yp + ys < yp || gp + gs < gp || upp + us < upp) return false;
+    // an exact alias (same start, same row stride) is element-wise safe
+    const bool ga = yp == gp && p.output_stride == p.gate_stride;
+    const bool ua = yp == upp && p.output_stride == p.up_stride;
+    // gate and up packed in one row: overlapping spans, disjoint elements
+    auto row_disjoint = [&](uintptr_t input, int stride) {
+        const size_t delta = yp > input ? yp - input : input - yp;
+        return (ga || ua) && stride == p.output_stride && delta >= (size_t)p.width * bytes &&
+               delta <= (size_t)stride - (size_t)p.width * bytes;
+    };
+    if ((!ga && yp < gp + gs && gp < yp + ys && !row_disjoint(gp, p.gate_stride)) ||
+        (!ua && yp < upp + us && upp < yp + ys && !row_disjoint(upp, p.up_stride)))
+        return false;
+    Kernel::Impl &s = *kernel.impl_;
+    if (s.id != -1 && s.id != id) return false;
+    s.id = id;
+    select(id);
+    DeviceState &d = state(id);
+    check((int)k200::launch_swiglu(y, gate, up, p.width, p.rows, p.gate_stride, p.up_stride, p.output_stride,
+                                   bytes == 2, d.info, d.stream));
+    check(wait());
+    return true;
+}
+
 Statistics statistics() {
     return {{devices[0].matmuls.load(), devices[1].matmuls.load()}, peer_copies.load(), peer_bytes.load()};
 }

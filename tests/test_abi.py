@@ -87,6 +87,9 @@ def test_cpp_api_symbols_match_reference_mangling(K):
         # row gathers (k200.h:339-343)
         "_ZN6kunlun12get_rows_f32ERNS_6KernelEiPvmPKvmPKimiii",
         "_ZN6kunlun18common_q4_get_rowsERNS_6KernelEiPvmRKNS_14CommonQ4WeightEPKimi",
+        # fused SwiGLU (k200.h:186-199)
+        "_ZN6kunlun13swiglu_reasonERKNS_12SwiGLULayoutE",
+        "_ZN6kunlun6swigluERNS_6KernelEiPvmPKvmS4_mRKNS_12SwiGLULayoutE",
     ]
     missing = [s for s in expected if s not in exported]
     assert not missing, missing
@@ -102,7 +105,7 @@ def test_reference_consumers_link_against_this_library():
     symbol from this library (built by `make -C oracle consumers`)."""
     bindir = os.path.join(ROOT, "oracle", "_ref", "bin")
     progs = [p for p in ("library-bench", "fused-bench", "native-q4-bench", "common-q4-bench", "get-rows-test",
-                         "get-rows-f32-test", "memory-example")
+                         "get-rows-f32-test", "swiglu-bench", "swiglu-contract", "memory-example")
              if os.path.exists(os.path.join(bindir, p))]
     if not progs:
         pytest.skip("reference consumer programs not built in this checkout")

@@ -123,3 +123,21 @@ def test_get_rows_test(K, O, gpu, tmp_path, k, n):
     assert "GET_ROWS_UNIT_PASS invalid_ids_rejected=1" in out, out
     assert out.count("bitwise=1") == 4, out
 
+
+# bench/swiglu-contract.cpp: eleven malformed calls rejected before any device
+# work or allocation.
+def test_swiglu_contract(K, gpu):
+    out = _run("swiglu-contract")
+    assert out.count("rejected_before_device=1 PASS") == 11, out
+
+
+# bench/swiglu-bench.cpp: PD WIDTH ROWS BYTES PATTERN PACKED GAP ALIAS; its own
+# bar (NMSE, max error, NaN/Inf rules, untouched padding) prints pass=1.
+@pytest.mark.parametrize("args", [(0, 11008, 128, 4, 0, 0, 0, 0), (0, 11008, 16, 2, 0, 0, 0, 0),
+                                  (0, 4096, 8, 4, 4, 0, 0, 0), (0, 4096, 8, 4, 5, 0, 0, 0),
+                                  (0, 1000, 5, 4, 2, 1, 0, 1), (0, 1000, 5, 2, 3, 1, 64, 2),
+                                  (0, 777, 3, 4, 0, 0, 32, 1)],
+                         ids=lambda a: "-".join(map(str, a)))
+def test_swiglu_bench(K, gpu, args):
+    out = _run("swiglu-bench", *args)
+    assert "pass=1" in out, out
