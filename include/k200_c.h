@@ -162,6 +162,44 @@ void k200_common_q4_quantization(void *workspace, const void **values, const voi
 /* out = {paths[0..7], calls, chunks} */
 void k200_common_q4_statistics(void *workspace, size_t out[10]);
 
+/* Activation lease and gate/up pair (kunlun::CommonQ4ActivationLease,
+   common_q4_prepare, common_q4_matmul_shared, common_q4_matmul_pair:
+   src/q4-activation.inc:1-98, src/q4-pair.inc:1-80).  The int results are
+   1 = done, 0 = declined (nothing written). */
+void *k200_common_q4_lease_create(void);
+void k200_common_q4_lease_destroy(void *lease);
+void k200_common_q4_lease_reset(void *lease);
+int k200_common_q4_lease_matches(void *lease, int device, int k, int rows, int type, uint64_t generation);
+size_t k200_common_q4_lease_chunks(void *lease);
+/* chunk `index`: *values, *scales, out = {first, rows, padded_rows, kp, components}, bytes = {values, scales} */
+void k200_common_q4_lease_chunk(void *lease, size_t index, const void **values, const void **scales, int out[5],
+                                size_t bytes[2]);
+int k200_common_q4_prepare(void *workspace, int device, const void *input, int k, int rows, int type,
+                           uint64_t generation, void *lease);
+int k200_common_q4_matmul_shared(void *workspace, int device, void *y, void *weight, void *lease, uint64_t generation);
+int k200_common_q4_matmul_pair(void *workspace, int device, void *y0, void *y1, void *weight0, void *weight1,
+                               void *lease, uint64_t generation);
+/* out = {calls, declined, l3_partial_bytes}; the last status is a kunlun::CommonQ4PairStatus value */
+void k200_common_q4_pair_statistics(void *workspace, size_t out[3]);
+int k200_common_q4_pair_last_status(void *workspace);
+/* out = {prepare_calls, quantized_chunks, quant_kernel_launches, prepared_matmuls, prepared_chunks,
+          invalidations, rejected_calls, hbm_activation_bytes} */
+void k200_common_q4_activation_statistics(void *workspace, size_t out[8]);
+
+/* Q6_K typed GEMV (kunlun::Q6KWeight, Q6KWorkspace, q6_k_matmul:
+   src/q6-k.inc:1-142).  type 0 = f32, 1 = f16 activations. */
+int k200_q6_k_supported(int k, int n);
+size_t k200_q6_k_size(int k, int n);
+void *k200_q6_k_weight_create(int device, int k, int n, void *storage, size_t bytes);
+void k200_q6_k_weight_destroy(void *weight);
+void k200_q6_k_weight_upload(void *weight, const void *q6, size_t bytes);
+void *k200_q6_k_weight_data(void *weight);
+void *k200_q6_k_workspace_create(void);
+void k200_q6_k_workspace_destroy(void *workspace);
+/* out = {calls, uploads or 0, upload_bytes or 0, workspace_bytes} of the workspace */
+void k200_q6_k_workspace_statistics(void *workspace, size_t out[4]);
+void k200_q6_k_matmul(void *workspace, int device, void *y, void *weight, const void *x, int m, int type);
+
 /* Row gathers; 1 = rows written, 0 = contract violation or an index outside
    [0, n) (no output written).  Replace kunlun::get_rows_f32
    (src/get-rows-f32.inc:1-29) and kunlun::common_q4_get_rows

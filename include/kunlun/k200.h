@@ -172,6 +172,13 @@ struct CommonQ4ActivationStatistics {
     size_t hbm_activation_bytes;
     uint64_t quantization_ns, preparation_ns;
 };
+struct CommonQ4ActivationChunk {
+    const void *values;
+    const void *scales;
+    int first, rows, padded_rows, kp, components;
+    size_t values_bytes, scales_bytes;
+};
+class CommonQ4ActivationLease;
 class CommonQ4Workspace;
 struct CommonQ4WeightStatistics {
     size_t uploads, upload_bytes;
@@ -194,6 +201,10 @@ private:
     Impl *impl_;
     friend void common_q4_matmul(class CommonQ4Workspace &, int, void *, const CommonQ4Weight &, const void *, int,
                                  InputType);
+    friend bool common_q4_matmul_pair(CommonQ4Workspace &, int, void *, void *, const CommonQ4Weight &,
+                                      const CommonQ4Weight &, const CommonQ4ActivationLease &, uint64_t);
+    friend bool common_q4_matmul_shared(class CommonQ4Workspace &, int, void *, const CommonQ4Weight &,
+                                        const CommonQ4ActivationLease &, uint64_t);
 };
 struct CommonQ4Statistics {
     // GEMV, Combined, Wide, Rows64, Rows128, Combo2, Combo4, exact CL.
@@ -207,6 +218,12 @@ struct CommonQ4Quantization {
     const void *values;
     const void *scales;
     int rows, kp, components;
+};
+struct CommonQ4PairStatistics {
+    size_t calls, declined, l3_partial_bytes;
+};
+enum class CommonQ4PairStatus {
+    NotAttempted, Success, Disabled, InvalidInput, Configuration, WeightAbi, Lease, Alias, Workspace
 };
 class CommonQ4Workspace {
 public:
@@ -222,13 +239,109 @@ public:
     struct Impl;
 private:
     Impl *impl_;
+    friend CommonQ4PairStatistics common_q4_pair_statistics(const CommonQ4Workspace &);
+    friend CommonQ4PairStatus common_q4_pair_last_status(const CommonQ4Workspace &);
+    friend bool common_q4_matmul_pair(CommonQ4Workspace &, int, void *, void *, const CommonQ4Weight &,
+                                      const CommonQ4Weight &, const CommonQ4ActivationLease &, uint64_t);
     friend void common_q4_matmul(CommonQ4Workspace &, int, void *, const CommonQ4Weight &, const void *, int,
                                  InputType);
+    friend bool common_q4_prepare(CommonQ4Workspace &, int, const void *, int, int, InputType, uint64_t,
+                                  CommonQ4ActivationLease &);
+    friend bool common_q4_matmul_shared(class CommonQ4Workspace &, int, void *, const CommonQ4Weight &,
+                                        const CommonQ4ActivationLease &, uint64_t);
 };
 // X [m,k], Y [m,n].  Completes before returning.  M = 1: two-component A8;
 // M > 1: one int8 scale per activation row (Row A8).
 void common_q4_matmul(CommonQ4Workspace &, int device, void *y, const CommonQ4Weight &, const void *input, int m,
                       InputType type = InputType::f32);
+
+// A snapshot of quantised activations in a workspace, valid until that
+// workspace quantises again (another prepare, a plain common_q4_matmul, a
+// reset or the workspace's destruction).  The owner passes a nonzero
+// generation it changes after writing the input.
+class CommonQ4ActivationLease {
+public:
+    CommonQ4ActivationLease();
+    ~CommonQ4ActivationLease();
+    CommonQ4ActivationLease(const CommonQ4ActivationLease &) = delete;
+    CommonQ4ActivationLease &operator=(const CommonQ4ActivationLease &) = delete;
+    void reset();
+    bool matches(int device, int k, int rows, InputType, uint64_t generation) const;
+    size_t chunks() const;
+    CommonQ4ActivationChunk chunk(size_t index) const;
+    struct Impl;
+private:
+    Impl *impl_;
+    friend bool common_q4_matmul_pair(CommonQ4Workspace &, int, void *, void *, const CommonQ4Weight &,
+                                      const CommonQ4Weight &, const CommonQ4ActivationLease &, uint64_t);
+    friend bool common_q4_prepare(CommonQ4Workspace &, int, const void *, int, int, InputType, uint64_t,
+                                  CommonQ4ActivationLease &);
+    friend bool common_q4_matmul_shared(CommonQ4Workspace &, int, void *, const CommonQ4Weight &,
+                                        const CommonQ4ActivationLease &, uint64_t);
+};
+// Quantises X [rows, k] once into the workspace and points the lease at it
+// (chunks of up to 128 rows).  False: unsupported descriptor, nothing done.
+bool common_q4_prepare(CommonQ4Workspace &, int device, const void *input, int k, int rows, InputType,
+                       uint64_t generation, CommonQ4ActivationLease &);
+// common_q4_matmul on the lease's activations; false: stale or mismatched
+// lease or a pointer contract violation, no output written.
+bool common_q4_matmul_shared(CommonQ4Workspace &, int device, void *y, const CommonQ4Weight &,
+                             const CommonQ4ActivationLease &, uint64_t generation);
+// y0 = X W0^T and y1 = X W1^T for one prepared F32 activation row and two
+// weights of the same shape (the 7B/1B gate and up projections), in one pass
+// over the activations.  False (with the reason in common_q4_pair_last_status)
+// when declined; outputs untouched.
+bool common_q4_matmul_pair(CommonQ4Workspace &, int device, void *y0, void *y1, const CommonQ4Weight &w0,
+                           const CommonQ4Weight &w1, const CommonQ4ActivationLease &, uint64_t generation);
+CommonQ4PairStatistics common_q4_pair_statistics(const CommonQ4Workspace &);
+CommonQ4PairStatus common_q4_pair_last_status(const CommonQ4Workspace &);
+
+// ---- Q6_K typed GEMV (reference k200.h:135-165) ----------------------------
+struct Q6KInfo {
+    uint32_t abi_version;
+    int device, k, n;
+    size_t scale_offset, payload_bytes;
+};
+struct Q6KStatistics {
+    size_t calls, uploads, upload_bytes, workspace_bytes;
+    double pack_ms, upload_ms;
+};
+bool q6_k_supported(int k, int n);
+size_t q6_k_size(int k, int n);
+class Q6KWeight {
+public:
+    // Borrowed storage must be 256-byte aligned; null storage allocates a Buffer.
+    Q6KWeight(int device, int k, int n, void *storage = nullptr, size_t bytes = 0);
+    ~Q6KWeight();
+    Q6KWeight(const Q6KWeight &) = delete;
+    Q6KWeight &operator=(const Q6KWeight &) = delete;
+    // Packs N rows of K/256 GGML Q6_K blocks on the host and uploads them.
+    void upload(const void *q6, size_t bytes);
+    Q6KInfo info() const;
+    Q6KStatistics statistics() const;
+    void *data() const;
+    struct Impl;
+private:
+    Impl *impl_;
+    friend void q6_k_matmul(class Q6KWorkspace &, int, void *, const Q6KWeight &, const void *, int, InputType);
+};
+class Q6KWorkspace {
+public:
+    Q6KWorkspace();
+    ~Q6KWorkspace();
+    Q6KWorkspace(const Q6KWorkspace &) = delete;
+    Q6KWorkspace &operator=(const Q6KWorkspace &) = delete;
+    Q6KStatistics statistics() const;
+    size_t legacy_calls() const;
+    struct Impl;
+private:
+    Impl *impl_;
+    friend void q6_k_matmul(Q6KWorkspace &, int, void *, const Q6KWeight &, const void *, int, InputType);
+};
+// X [m,k] (m = 1..512), Y [m,n]; activations quantised per 256-value chunk.
+// Completes before returning.
+void q6_k_matmul(Q6KWorkspace &, int device, void *y, const Q6KWeight &, const void *x, int m = 1,
+                 InputType type = InputType::f32);
 
 // Row gathers: output[r] = input row indices[r] (F32 rows; K % 16 == 0,
 // 16 <= K <= 1048576) or the decoded common-Q4 weight column indices[r]

@@ -94,6 +94,32 @@ _SIGNATURES = {
                                     C.c_size_t, C.c_int, C.c_int, C.c_int]),
     "k200_common_q4_get_rows": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p,
                                           C.c_size_t, C.c_int]),
+    "k200_common_q4_lease_create": (C.c_void_p, []),
+    "k200_common_q4_lease_destroy": (None, [C.c_void_p]),
+    "k200_common_q4_lease_reset": (None, [C.c_void_p]),
+    "k200_common_q4_lease_matches": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_uint64]),
+    "k200_common_q4_lease_chunks": (C.c_size_t, [C.c_void_p]),
+    "k200_common_q4_lease_chunk": (None, [C.c_void_p, C.c_size_t, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
+                                          C.POINTER(C.c_int), C.POINTER(C.c_size_t)]),
+    "k200_common_q4_prepare": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_uint64,
+                                         C.c_void_p]),
+    "k200_common_q4_matmul_shared": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                               C.c_uint64]),
+    "k200_common_q4_matmul_pair": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                             C.c_void_p, C.c_uint64]),
+    "k200_common_q4_pair_statistics": (None, [C.c_void_p, C.POINTER(C.c_size_t)]),
+    "k200_common_q4_pair_last_status": (C.c_int, [C.c_void_p]),
+    "k200_common_q4_activation_statistics": (None, [C.c_void_p, C.POINTER(C.c_size_t)]),
+    "k200_q6_k_supported": (C.c_int, [C.c_int, C.c_int]),
+    "k200_q6_k_size": (C.c_size_t, [C.c_int, C.c_int]),
+    "k200_q6_k_weight_create": (C.c_void_p, [C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_size_t]),
+    "k200_q6_k_weight_destroy": (None, [C.c_void_p]),
+    "k200_q6_k_weight_upload": (None, [C.c_void_p, C.c_void_p, C.c_size_t]),
+    "k200_q6_k_weight_data": (C.c_void_p, [C.c_void_p]),
+    "k200_q6_k_workspace_create": (C.c_void_p, []),
+    "k200_q6_k_workspace_destroy": (None, [C.c_void_p]),
+    "k200_q6_k_workspace_statistics": (None, [C.c_void_p, C.POINTER(C.c_size_t)]),
+    "k200_q6_k_matmul": (None, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int]),
     "k200_swiglu_reason": (C.c_char_p, [C.c_int] * 6),
     "k200_swiglu": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_void_p,
                               C.c_size_t] + [C.c_int] * 6),
@@ -473,6 +499,13 @@ class CommonQ4Workspace:
         lib().k200_common_q4_statistics(self.handle, out)
         return {"paths": list(out[:8]), "calls": out[8], "chunks": out[9]}
 
+    def activation_statistics(self) -> dict:
+        out = (C.c_size_t * 8)()
+        lib().k200_common_q4_activation_statistics(self.handle, out)
+        names = ("prepare_calls", "quantized_chunks", "quant_kernel_launches", "prepared_matmuls",
+                 "prepared_chunks", "invalidations", "rejected_calls", "hbm_activation_bytes")
+        return dict(zip(names, out))
+
     def close(self) -> None:
         if self.handle:
             lib().k200_common_q4_workspace_destroy(self.handle)
@@ -489,6 +522,139 @@ def common_q4_matmul(workspace: CommonQ4Workspace, device: int, y, weight: Commo
                      type: int = INPUT_F32) -> None:
     """Y [m,n] = X [m,k] . W^T; completes before returning (M=1: two-component A8, M>1: Row A8)."""
     lib().k200_common_q4_matmul(workspace.handle, device, _ptr(y), weight.handle, _ptr(x), m, int(type))
+
+
+def q6_k_supported(k: int, n: int) -> bool:
+    return bool(lib().k200_q6_k_supported(k, n))
+
+
+def q6_k_size(k: int, n: int) -> int:
+    return lib().k200_q6_k_size(k, n)
+
+
+class Q6KWeight:
+    """kunlun::Q6KWeight (k200.h:139-147): GGML Q6_K rows packed for the device."""
+
+    def __init__(self, device: int, k: int, n: int, storage=None, nbytes: int = 0):
+        self.handle = lib().k200_q6_k_weight_create(device, k, n, _ptr(storage), nbytes)
+
+    def upload(self, q6: np.ndarray) -> None:
+        src = np.ascontiguousarray(q6, np.uint8)
+        lib().k200_q6_k_weight_upload(self.handle, _ptr(src), src.nbytes)
+
+    def data(self) -> int:
+        return lib().k200_q6_k_weight_data(self.handle)
+
+    def close(self) -> None:
+        if self.handle:
+            lib().k200_q6_k_weight_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Q6KWorkspace:
+    """kunlun::Q6KWorkspace (k200.h:150-159)."""
+
+    def __init__(self):
+        self.handle = lib().k200_q6_k_workspace_create()
+
+    def statistics(self) -> dict:
+        out = (C.c_size_t * 4)()
+        lib().k200_q6_k_workspace_statistics(self.handle, out)
+        return {"calls": out[0], "workspace_bytes": out[3]}
+
+    def close(self) -> None:
+        if self.handle:
+            lib().k200_q6_k_workspace_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def q6_k_matmul(workspace: Q6KWorkspace, device: int, y, weight: Q6KWeight, x, m: int = 1,
+                type: int = INPUT_F32) -> None:
+    """kunlun::q6_k_matmul (src/q6-k.inc:104-142): completes before returning."""
+    lib().k200_q6_k_matmul(workspace.handle, device, _ptr(y), weight.handle, _ptr(x), m, int(type))
+
+
+# kunlun::CommonQ4PairStatus values (k200.h:281)
+PAIR_STATUS = ("NotAttempted", "Success", "Disabled", "InvalidInput", "Configuration", "WeightAbi", "Lease", "Alias",
+               "Workspace")
+
+
+class CommonQ4ActivationLease:
+    """kunlun::CommonQ4ActivationLease (k200.h:310-328): a snapshot of one workspace's quantised activations."""
+
+    def __init__(self):
+        self.handle = lib().k200_common_q4_lease_create()
+
+    def reset(self) -> None:
+        lib().k200_common_q4_lease_reset(self.handle)
+
+    def matches(self, device: int, k: int, rows: int, type: int, generation: int) -> bool:
+        return bool(lib().k200_common_q4_lease_matches(self.handle, device, k, rows, int(type), generation))
+
+    def chunks(self) -> int:
+        return lib().k200_common_q4_lease_chunks(self.handle)
+
+    def chunk(self, index: int) -> dict:
+        values, scales = C.c_void_p(), C.c_void_p()
+        out, nb = (C.c_int * 5)(), (C.c_size_t * 2)()
+        lib().k200_common_q4_lease_chunk(self.handle, index, C.byref(values), C.byref(scales), out, nb)
+        return {"values": values.value, "scales": scales.value, "first": out[0], "rows": out[1],
+                "padded_rows": out[2], "kp": out[3], "components": out[4], "values_bytes": nb[0],
+                "scales_bytes": nb[1]}
+
+    def close(self) -> None:
+        if self.handle:
+            lib().k200_common_q4_lease_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def common_q4_prepare(workspace: "CommonQ4Workspace", device: int, x, k: int, rows: int, type: int,
+                      generation: int, lease: CommonQ4ActivationLease) -> bool:
+    """kunlun::common_q4_prepare (src/q4-activation.inc:31-76)."""
+    return bool(lib().k200_common_q4_prepare(workspace.handle, device, _ptr(x), k, rows, int(type), generation,
+                                             lease.handle))
+
+
+def common_q4_matmul_shared(workspace: "CommonQ4Workspace", device: int, y, weight: "CommonQ4Weight",
+                            lease: CommonQ4ActivationLease, generation: int) -> bool:
+    """kunlun::common_q4_matmul_shared (src/q4-activation.inc:79-98)."""
+    return bool(lib().k200_common_q4_matmul_shared(workspace.handle, device, _ptr(y), weight.handle, lease.handle,
+                                                   generation))
+
+
+def common_q4_matmul_pair(workspace: "CommonQ4Workspace", device: int, y0, y1, w0: "CommonQ4Weight",
+                          w1: "CommonQ4Weight", lease: CommonQ4ActivationLease, generation: int) -> bool:
+    """kunlun::common_q4_matmul_pair (src/q4-pair.inc:9-80)."""
+    return bool(lib().k200_common_q4_matmul_pair(workspace.handle, device, _ptr(y0), _ptr(y1), w0.handle, w1.handle,
+                                                 lease.handle, generation))
+
+
+def common_q4_pair_statistics(workspace: "CommonQ4Workspace") -> dict:
+    out = (C.c_size_t * 3)()
+    lib().k200_common_q4_pair_statistics(workspace.handle, out)
+    return {"calls": out[0], "declined": out[1], "l3_partial_bytes": out[2]}
+
+
+def common_q4_pair_last_status(workspace: "CommonQ4Workspace") -> str:
+    return PAIR_STATUS[lib().k200_common_q4_pair_last_status(workspace.handle)]
 
 
 def get_rows_f32(kernel: Kernel, device: int, output, output_bytes: int, input, input_bytes: int, indices,

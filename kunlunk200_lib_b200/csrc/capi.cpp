@@ -217,6 +217,100 @@ int k200_get_rows_f32(void *kernel, int device, void *output, size_t output_byte
                : 0;
 }
 
+void *k200_common_q4_lease_create(void) { return new kunlun::CommonQ4ActivationLease(); }
+void k200_common_q4_lease_destroy(void *lease) { delete static_cast<kunlun::CommonQ4ActivationLease *>(lease); }
+void k200_common_q4_lease_reset(void *lease) { static_cast<kunlun::CommonQ4ActivationLease *>(lease)->reset(); }
+int k200_common_q4_lease_matches(void *lease, int device, int k, int rows, int type, uint64_t generation) {
+    return static_cast<kunlun::CommonQ4ActivationLease *>(lease)->matches(device, k, rows,
+                                                                         static_cast<kunlun::InputType>(type),
+                                                                         generation)
+               ? 1
+               : 0;
+}
+size_t k200_common_q4_lease_chunks(void *lease) { return static_cast<kunlun::CommonQ4ActivationLease *>(lease)->chunks(); }
+void k200_common_q4_lease_chunk(void *lease, size_t index, const void **values, const void **scales, int out[5],
+                                size_t bytes[2]) {
+    kunlun::require(lease && values && scales && out && bytes);
+    const kunlun::CommonQ4ActivationChunk c = static_cast<kunlun::CommonQ4ActivationLease *>(lease)->chunk(index);
+    *values = c.values;
+    *scales = c.scales;
+    out[0] = c.first;
+    out[1] = c.rows;
+    out[2] = c.padded_rows;
+    out[3] = c.kp;
+    out[4] = c.components;
+    bytes[0] = c.values_bytes;
+    bytes[1] = c.scales_bytes;
+}
+int k200_common_q4_prepare(void *workspace, int device, const void *input, int k, int rows, int type,
+                           uint64_t generation, void *lease) {
+    return kunlun::common_q4_prepare(*static_cast<kunlun::CommonQ4Workspace *>(workspace), device, input, k, rows,
+                                     static_cast<kunlun::InputType>(type), generation,
+                                     *static_cast<kunlun::CommonQ4ActivationLease *>(lease))
+               ? 1
+               : 0;
+}
+int k200_common_q4_matmul_shared(void *workspace, int device, void *y, void *weight, void *lease, uint64_t generation) {
+    return kunlun::common_q4_matmul_shared(*static_cast<kunlun::CommonQ4Workspace *>(workspace), device, y,
+                                           *static_cast<kunlun::CommonQ4Weight *>(weight),
+                                           *static_cast<kunlun::CommonQ4ActivationLease *>(lease), generation)
+               ? 1
+               : 0;
+}
+int k200_common_q4_matmul_pair(void *workspace, int device, void *y0, void *y1, void *weight0, void *weight1,
+                               void *lease, uint64_t generation) {
+    return kunlun::common_q4_matmul_pair(*static_cast<kunlun::CommonQ4Workspace *>(workspace), device, y0, y1,
+                                         *static_cast<kunlun::CommonQ4Weight *>(weight0),
+                                         *static_cast<kunlun::CommonQ4Weight *>(weight1),
+                                         *static_cast<kunlun::CommonQ4ActivationLease *>(lease), generation)
+               ? 1
+               : 0;
+}
+void k200_common_q4_pair_statistics(void *workspace, size_t out[3]) {
+    kunlun::require(workspace && out);
+    const kunlun::CommonQ4PairStatistics s =
+        kunlun::common_q4_pair_statistics(*static_cast<kunlun::CommonQ4Workspace *>(workspace));
+    out[0] = s.calls;
+    out[1] = s.declined;
+    out[2] = s.l3_partial_bytes;
+}
+int k200_common_q4_pair_last_status(void *workspace) {
+    return static_cast<int>(kunlun::common_q4_pair_last_status(*static_cast<kunlun::CommonQ4Workspace *>(workspace)));
+}
+void k200_common_q4_activation_statistics(void *workspace, size_t out[8]) {
+    kunlun::require(workspace && out);
+    const kunlun::CommonQ4ActivationStatistics s =
+        static_cast<kunlun::CommonQ4Workspace *>(workspace)->activation_statistics();
+    const size_t v[8] = {s.prepare_calls,   s.quantized_chunks, s.quant_kernel_launches, s.prepared_matmuls,
+                         s.prepared_chunks, s.invalidations,    s.rejected_calls,        s.hbm_activation_bytes};
+    for (int i = 0; i < 8; ++i) out[i] = v[i];
+}
+
+int k200_q6_k_supported(int k, int n) { return kunlun::q6_k_supported(k, n) ? 1 : 0; }
+size_t k200_q6_k_size(int k, int n) { return kunlun::q6_k_size(k, n); }
+void *k200_q6_k_weight_create(int device, int k, int n, void *storage, size_t bytes) {
+    return new kunlun::Q6KWeight(device, k, n, storage, bytes);
+}
+void k200_q6_k_weight_destroy(void *weight) { delete static_cast<kunlun::Q6KWeight *>(weight); }
+void k200_q6_k_weight_upload(void *weight, const void *q6, size_t bytes) {
+    static_cast<kunlun::Q6KWeight *>(weight)->upload(q6, bytes);
+}
+void *k200_q6_k_weight_data(void *weight) { return static_cast<kunlun::Q6KWeight *>(weight)->data(); }
+void *k200_q6_k_workspace_create(void) { return new kunlun::Q6KWorkspace(); }
+void k200_q6_k_workspace_destroy(void *workspace) { delete static_cast<kunlun::Q6KWorkspace *>(workspace); }
+void k200_q6_k_workspace_statistics(void *workspace, size_t out[4]) {
+    kunlun::require(workspace && out);
+    const kunlun::Q6KStatistics s = static_cast<kunlun::Q6KWorkspace *>(workspace)->statistics();
+    out[0] = s.calls;
+    out[1] = s.uploads;
+    out[2] = s.upload_bytes;
+    out[3] = s.workspace_bytes;
+}
+void k200_q6_k_matmul(void *workspace, int device, void *y, void *weight, const void *x, int m, int type) {
+    kunlun::q6_k_matmul(*static_cast<kunlun::Q6KWorkspace *>(workspace), device, y,
+                        *static_cast<kunlun::Q6KWeight *>(weight), x, m, static_cast<kunlun::InputType>(type));
+}
+
 const char *k200_swiglu_reason(int width, int rows, int gate_stride, int up_stride, int output_stride, int type) {
     const kunlun::SwiGLULayout p{width, rows, gate_stride, up_stride, output_stride,
                                  static_cast<kunlun::InputType>(type)};

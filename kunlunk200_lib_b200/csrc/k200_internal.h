@@ -61,6 +61,11 @@ cudaError_t launch_get_rows_f32(float *out, const float *in, const int32_t *idx,
                                 cudaStream_t stream);
 cudaError_t launch_common_get_rows(float *out, const uint8_t *w, size_t scale_offset, int kp, int np,
                                    const int32_t *idx, int *status, int k, int n, int rows, cudaStream_t stream);
+// Q6_K typed GEMV (q6_k.cu): chunk-256 A8 of one activation row, then the
+// int8 x int8 GEMV over the packed weights (n % 32 == 0, k % 256 == 0).
+cudaError_t launch_q6_quant(const void *x, int dtype, int k, int8_t *q, float *scales, cudaStream_t stream);
+cudaError_t launch_q6_gemv(float *y, const int8_t *w, const float *wscale, const int8_t *q, const float *ascale, int k,
+                           int n, const DeviceInfo &dev, cudaStream_t stream);
 // kunlun::swiglu (swiglu.cu): y = SiLU(gate) * up, strides in bytes, f16 != 0: F16 rows.
 cudaError_t launch_swiglu(void *y, const void *gate, const void *up, int width, int rows, int gs, int us, int ys,
                           int f16, const DeviceInfo &dev, cudaStream_t stream);
@@ -112,6 +117,9 @@ cudaError_t launch_common_gemv_a8x2(const uint8_t *w, size_t scale_offset, int k
                                     const int8_t *q1, const float *params, int k, int n, float *y,
                                     const DeviceInfo &dev, cudaStream_t stream);
 // row_scale: one scale every 16 floats (the activation view's layout).
+cudaError_t launch_common_gemv_pair(const uint8_t *w0, const uint8_t *w1, size_t scale_offset, int kp, int np,
+                                    const int8_t *q0, const int8_t *q1, const float *params, int k, int n, float *y0,
+                                    float *y1, const DeviceInfo &dev, cudaStream_t stream);
 cudaError_t launch_common_gemm_a8(const uint8_t *w, size_t scale_offset, int kp, int np, const int8_t *q,
                                   const float *row_scale, int k, int n, int m, float *y, cudaStream_t stream);
 

@@ -235,10 +235,13 @@ __device__ __forceinline__ void common_unpack(uint32_t u, uint32_t &e0, uint32_t
 }
 
 // M = 1: W4A8x2 GEMV, lane = column.  The components come in the activation
-// view layout (block b's 32 values at b*64), zero past k.
-__global__ void __launch_bounds__(256) common_gemv_a8x2_kernel(const uint8_t *w, size_t scale_offset, int kp, int np,
-                                                                const int8_t *q0g, const int8_t *q1g,
-                                                                const float *params, int k, int n, float *y) {
+// view layout (block b's 32 values at b*64), zero past k.  With a second
+// weight (w1, y1: the gate/up pair) the same activation records serve both:
+// tiles [0, T) of the grid walk belong to w and [T, 2T) to w1.
+__global__ void __launch_bounds__(256) common_gemv_a8x2_kernel(const uint8_t *w, const uint8_t *w1, size_t scale_offset,
+                                                                int kp, int np, const int8_t *q0g, const int8_t *q1g,
+                                                                const float *params, int k, int n, float *y,
+                                                                float *y1) {
     extern __shared__ int qw[];  // [2][kp/4] int8x4 words, blocks packed densely
     const int words = kp / 4;
     for (int i = threadIdx.x; i < words; i += blockDim.x) {
@@ -248,14 +251,18 @@ __global__ void __launch_bounds__(256) common_gemv_a8x2_kernel(const uint8_t *w,
     }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, warps = blockDim.x >> 5;
-    const int blocks = (k + 31) / 32, tiles = (n + 31) / 32;
+    const int blocks = (k + 31) / 32, tiles = (n + 31) / 32, walk = w1 ? 2 * tiles : tiles;
     const float s0 = params[0], s1 = params[1];
-    const uint16_t *sc = reinterpret_cast<const uint16_t *>(w + scale_offset);
-    for (int tile = blockIdx.x * warps + warp; tile < tiles; tile += gridDim.x * warps) {
+    for (int t = blockIdx.x * warps + warp; t < walk; t += gridDim.x * warps) {
+        const bool second = t >= tiles;
+        const int tile = second ? t - tiles : t;
+        const uint8_t *ww = second ? w1 : w;
+        float *yy = second ? y1 : y;
+        const uint16_t *sc = reinterpret_cast<const uint16_t *>(ww + scale_offset);
         const int col = tile * 32 + lane;
         float sum = 0.f;
         for (int kb = 0; kb < blocks; ++kb) {
-            const uint4 v = common_block(w, kp, col, kb);
+            const uint4 v = common_block(ww, kp, col, kb);
             const float d = half_bits(__ldg(sc + static_cast<size_t>(kb) * np + col));
             const int *a0 = qw + kb * 8, *a1 = qw + words + kb * 8;
             int dot0 = 0, dot1 = 0;
@@ -271,7 +278,7 @@ __global__ void __launch_bounds__(256) common_gemv_a8x2_kernel(const uint8_t *w,
             }
             sum = __fadd_rn(sum, a8x2_partial(dot0, dot1, s0, s1, d));
         }
-        if (col < n) y[col] = sum;
+        if (col < n) yy[col] = sum;
     }
 }
 
@@ -368,8 +375,18 @@ cudaError_t launch_common_gemv_a8x2(const uint8_t *w, size_t scale_offset, int k
                                     const DeviceInfo &dev, cudaStream_t stream) {
     const size_t smem = 2 * static_cast<size_t>(kp);
     const int tiles = (n + 31) / 32;
-    common_gemv_a8x2_kernel<<<grid_for(tiles, 8, dev), 256, smem, stream>>>(w, scale_offset, kp, np, q0, q1, params,
-                                                                           k, n, y);
+    common_gemv_a8x2_kernel<<<grid_for(tiles, 8, dev), 256, smem, stream>>>(w, nullptr, scale_offset, kp, np, q0, q1,
+                                                                           params, k, n, y, nullptr);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_common_gemv_pair(const uint8_t *w0, const uint8_t *w1, size_t scale_offset, int kp, int np,
+                                    const int8_t *q0, const int8_t *q1, const float *params, int k, int n, float *y0,
+                                    float *y1, const DeviceInfo &dev, cudaStream_t stream) {
+    const size_t smem = 2 * static_cast<size_t>(kp);
+    const int tiles = (n + 31) / 32;
+    common_gemv_a8x2_kernel<<<grid_for(2 * tiles, 8, dev), 256, smem, stream>>>(w0, w1, scale_offset, kp, np, q0, q1,
+                                                                               params, k, n, y0, y1);
     return cudaGetLastError();
 }
 

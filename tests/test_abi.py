@@ -87,6 +87,25 @@ def test_cpp_api_symbols_match_reference_mangling(K):
         # row gathers (k200.h:339-343)
         "_ZN6kunlun12get_rows_f32ERNS_6KernelEiPvmPKvmPKimiii",
         "_ZN6kunlun18common_q4_get_rowsERNS_6KernelEiPvmRKNS_14CommonQ4WeightEPKimi",
+        # activation lease and gate/up pair (k200.h:310-383)
+        "_ZN6kunlun17common_q4_prepareERNS_17CommonQ4WorkspaceEiPKviiNS_9InputTypeEmRNS_23CommonQ4ActivationLeaseE",
+        "_ZN6kunlun23common_q4_matmul_sharedERNS_17CommonQ4WorkspaceEiPvRKNS_14CommonQ4WeightERKNS_23CommonQ4ActivationLeaseEm",
+        "_ZN6kunlun21common_q4_matmul_pairERNS_17CommonQ4WorkspaceEiPvS2_RKNS_14CommonQ4WeightES5_RKNS_23CommonQ4ActivationLeaseEm",
+        "_ZN6kunlun25common_q4_pair_statisticsERKNS_17CommonQ4WorkspaceE",
+        "_ZN6kunlun26common_q4_pair_last_statusERKNS_17CommonQ4WorkspaceE",
+        "_ZN6kunlun23CommonQ4ActivationLeaseC1Ev",
+        "_ZN6kunlun23CommonQ4ActivationLease5resetEv",
+        "_ZNK6kunlun23CommonQ4ActivationLease7matchesEiiiNS_9InputTypeEm",
+        "_ZNK6kunlun23CommonQ4ActivationLease6chunksEv",
+        "_ZNK6kunlun23CommonQ4ActivationLease5chunkEm",
+        # Q6_K typed GEMV (k200.h:135-165)
+        "_ZN6kunlun14q6_k_supportedEii",
+        "_ZN6kunlun9q6_k_sizeEii",
+        "_ZN6kunlun9Q6KWeightC1EiiiPvm",
+        "_ZN6kunlun9Q6KWeight6uploadEPKvm",
+        "_ZN6kunlun12Q6KWorkspaceC1Ev",
+        "_ZNK6kunlun12Q6KWorkspace12legacy_callsEv",
+        "_ZN6kunlun11q6_k_matmulERNS_12Q6KWorkspaceEiPvRKNS_9Q6KWeightEPKviNS_9InputTypeE",
         # fused SwiGLU (k200.h:186-199)
         "_ZN6kunlun13swiglu_reasonERKNS_12SwiGLULayoutE",
         "_ZN6kunlun6swigluERNS_6KernelEiPvmPKvmS4_mRKNS_12SwiGLULayoutE",
@@ -104,8 +123,9 @@ def test_reference_consumers_link_against_this_library():
     """Reference programs compiled against the reference header resolve every
     symbol from this library (built by `make -C oracle consumers`)."""
     bindir = os.path.join(ROOT, "oracle", "_ref", "bin")
-    progs = [p for p in ("library-bench", "fused-bench", "native-q4-bench", "common-q4-bench", "get-rows-test",
-                         "get-rows-f32-test", "swiglu-bench", "swiglu-contract", "memory-example")
+    progs = [p for p in ("library-bench", "fused-bench", "native-q4-bench", "common-q4-bench",
+                         "common-q4-state-bench", "get-rows-test",
+                         "get-rows-f32-test", "swiglu-bench", "swiglu-contract", "q6-k-test", "memory-example")
              if os.path.exists(os.path.join(bindir, p))]
     if not progs:
         pytest.skip("reference consumer programs not built in this checkout")

@@ -141,3 +141,25 @@ def test_swiglu_contract(K, gpu):
 def test_swiglu_bench(K, gpu, args):
     out = _run("swiglu-bench", *args)
     assert "pass=1" in out, out
+
+
+# bench/common-q4-state-bench.cpp: PD F16.  80 calls on one workspace over
+# M in {1, 8, 32, 64, 128, 129, 256}: outputs equal those of fresh workspaces,
+# the weight pointer and device allocation stay put after the first round.
+@pytest.mark.parametrize("f16", [0, 1])
+def test_common_q4_state_bench(K, gpu, f16):
+    out = _run("common-q4-state-bench", 0, f16)
+    assert '"correct":true' in out and '"stable_hbm":true' in out, out
+
+
+# bench/q6-k-test.cpp: FILE OFFSET K N PD.  Implementation NMSE < 1e-10 against
+# its FP64 restatement over the chunk-256 A8 activations, repeat runs bitwise
+# equal, zero input gives zero output, and guards untouched.
+@pytest.mark.parametrize("k,n", [(4096, 4096), (256, 32), (2048, 11008)])
+def test_q6_k_test(K, gpu, tmp_path, k, n):
+    from test_q6_k import q6_blocks
+    path = tmp_path / "weights.q6k"
+    path.write_bytes(b"\0" * 32 + q6_blocks(7, k, n).tobytes())
+    out = _run("q6-k-test", str(path), 32, k, n, 0)
+    assert "Q6_STANDALONE_PASS" in out and "Q6_CHUNK_SCALE_PASS" in out, out
+
