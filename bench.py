@@ -293,29 +293,71 @@ def run_ours(args) -> None:
         x = torch.rand(UP[0], generator=gen, device="cuda") * 2 - 1
         y1_full = torch.empty(UP[1], device="cuda")
         y2_full = torch.empty(DOWN[1], device="cuda")
-        y1_shard = y1_full if world == 1 else torch.empty(n_up, device="cuda")
-        y2_shard = y2_full if world == 1 else torch.empty(n_down, device="cuda")
     stream.synchronize()
     kern = K.Kernel()
 
-    def step(s: int, xin=None):
-        wu, wd = weights[s % sets]
-        K.matmul(kern, dev, y1_shard, wu, x if xin is None else xin, UP[0], n_up, 1, K.Q4_0)
-        if world > 1:
-            dist.all_gather_into_tensor(y1_full, y1_shard)
-        K.matmul(kern, dev, y2_shard, wd, y1_full, DOWN[0], n_down, 1, K.Q4_0)
-        if world > 1:
-            dist.all_gather_into_tensor(y2_full, y2_shard)
+    # N > 1: each GEMV stores its rows into every rank's output over NVLink
+    # (k200_matmul_q4_gather); the down GEMV waits on the device for every
+    # rank's up rows.  Outputs alternate between two buffers by step parity.
+    if world > 1:
+        from kunlunk200_lib_b200.shard import PeerExchange
 
+        def all_gather_obj(obj):
+            got = [None] * world
+            dist.all_gather_object(got, obj)
+            return got
+
+        ex_up = PeerExchange.over_group(K, dev, UP[1], world, rank, all_gather_obj)
+        ex_down = PeerExchange.over_group(K, dev, DOWN[1], world, rank, all_gather_obj)
+        up_begin, down_begin = row_shard(UP[1], world, rank)[0], row_shard(DOWN[1], world, rank)[0]
+        scratch_bytes = max(K.matmul_q4_gather_scratch(dev, UP[0], n_up),
+                            K.matmul_q4_gather_scratch(dev, DOWN[0], n_down))
+        if not scratch_bytes:
+            raise SystemExit("shard shape not handled by the batch-1 tensor-core GEMV")
+        scratch = torch.zeros(scratch_bytes, dtype=torch.uint8, device="cuda")
+
+    def gemv_up(s: int):
+        wu = weights[s % sets][0]
+        if world == 1:
+            K.matmul(kern, dev, y1_full, wu, x, UP[0], n_up, 1, K.Q4_0)
+            return
+        K.check(K.matmul_q4_gather(dev, ex_up.view(s), up_begin, wu, x, UP[0], n_up, scratch, scratch_bytes))
+
+    def gemv_down(s: int):
+        wd = weights[s % sets][1]
+        if world == 1:
+            K.matmul(kern, dev, y2_full, wd, y1_full, DOWN[0], n_down, 1, K.Q4_0)
+            return
+        K.check(K.matmul_q4_gather(dev, ex_down.view(s), down_begin, wd, ex_up.output(s), DOWN[0], n_down, scratch,
+                                   scratch_bytes, wait_for=ex_up.view(s)))
+
+    def step(s: int):
+        gemv_up(s)
+        gemv_down(s)
+
+    def output(s: int) -> int:
+        """Address of step s's full Y on this rank (complete after finish(s))."""
+        return y2_full.data_ptr() if world == 1 else ex_down.output(s)
+
+    def finish(s: int):
+        """N > 1: wait on the device until every rank's rows of step s's Y are here."""
+        if world > 1:
+            K.check(K.gather_wait(dev, ex_down.view(s)))
+
+    nwarm = max(3, args.warmup)
     with torch.cuda.stream(stream):
-        for i in range(max(3, args.warmup)):
+        for i in range(nwarm):
             step(i)
+        finish(nwarm - 1)
     stream.synchronize()
     K.check(K.wait())
+    if world > 1:
+        dist.barrier()  # the next sequence starts again at buffer 0
 
     # one CUDA graph holds a whole number of rotations; the timed region
     # replays it until exactly `steps` steps ran (a remainder graph if needed)
     per_graph = sets * max(1, 48 // sets)
+    per_graph *= 1 + per_graph % 2  # even: the output buffers alternate across replays
     reps, rem = divmod(args.steps, per_graph)
 
     def capture(nsteps: int):
@@ -325,6 +367,7 @@ def run_ours(args) -> None:
         with torch.cuda.graph(g, stream=stream):
             for i in range(nsteps):
                 step(i)
+            finish(nsteps - 1)
         return g
 
     g_main = capture(per_graph) if reps else None
@@ -335,6 +378,7 @@ def run_ours(args) -> None:
         if g_rem is not None:
             g_rem.replay()
     stream.synchronize()
+    K.check(K.wait())
 
     visible = os.environ.get("CUDA_VISIBLE_DEVICES")
     phys = int(visible.split(",")[dev]) if visible and visible.split(",")[dev].strip().isdigit() else dev
@@ -368,7 +412,7 @@ def run_ours(args) -> None:
     ms = float(t.item())
     clock_info = clocks.stop() if rank == 0 else None
     value = total_bytes * args.steps / (ms * 1e-3) / 1e9
-    launches = args.steps * 2
+    launches = args.steps * 2 + (reps + (1 if rem else 0)) * (world > 1)
 
     # ---- per-launch durations of the dominant kernel (events around each launch,
     #      queued behind a sleep so the GPU runs them back to back)
@@ -378,20 +422,22 @@ def run_ours(args) -> None:
         torch.cuda._sleep(20_000_000)
         evs[0].record(stream)
         for i in range(nprobe):
-            wu, wd = weights[i % sets]
-            K.matmul(kern, dev, y1_shard, wu, x, UP[0], n_up, 1, K.Q4_0)
+            gemv_up(i)
             evs[2 * i + 1].record(stream)
-            K.matmul(kern, dev, y2_shard, wd, y1_full, DOWN[0], n_down, 1, K.Q4_0)
+            gemv_down(i)
             evs[2 * i + 2].record(stream)
+        finish(nprobe - 1)
     stream.synchronize()
+    K.check(K.wait())
     d_up = [evs[2 * i].elapsed_time(evs[2 * i + 1]) for i in range(nprobe)]
     d_down = [evs[2 * i + 1].elapsed_time(evs[2 * i + 2]) for i in range(nprobe)]
     alg_up = q4_bytes(UP[0], n_up) + 4 * UP[0] + 4 * n_up
     alg_down = q4_bytes(DOWN[0], n_down) + 4 * DOWN[0] + 4 * n_down
     mean_up, mean_down = statistics.mean(d_up), statistics.mean(d_down)
-    # the timed region runs nothing but the two GEMV launches per step, so its
-    # average launch duration is the region's device time over its launches
-    launch_ms = ms / launches
+    # the timed region runs nothing but the two GEMV launches per step (and,
+    # on N > 1, one wait launch per graph), so its average GEMV duration is
+    # the region's device time over its GEMV launches
+    launch_ms = ms / (args.steps * 2)
     achieved = (alg_up + alg_down) / 2 / (launch_ms * 1e-3) / 1e9
     peaks = read_peaks()
 
@@ -410,7 +456,8 @@ def run_ours(args) -> None:
         for i in range(e2e_steps):
             K.check(K.copy_async(x, xh, xh.numel() * 4, K.HOST_TO_DEVICE))
             step(i)
-            K.check(K.copy_async(yh, y2_full, yh.numel() * 4, K.DEVICE_TO_HOST))
+            finish(i)
+            K.check(K.copy_async(yh, output(i), yh.numel() * 4, K.DEVICE_TO_HOST))
             K.check(K.wait())
         e1.record(stream)
     stream.synchronize()
@@ -432,7 +479,7 @@ def run_ours(args) -> None:
             "data": "synthetic",
             "config": {"workload": "q4_0 GEMV 7B MLP up+down, batch 1 (config 1)",
                        "up": "K4096xN11008", "down": "K11008xN4096", "batch": 1,
-                       "parallelism": f"row-shard{world}+allgather" if world > 1 else "single",
+                       "parallelism": f"row-shard{world}+fused-p2p-allgather" if world > 1 else "single",
                        "weights": "resident, declared static (k200_set_static_weights)",
                        "weight_bytes_per_step": total_bytes,
                        "l2": f"{sets} rotating weight sets ({sets * shard_bytes / 1e6:.0f} MB per GPU > 2x L2 "
@@ -449,15 +496,23 @@ def run_ours(args) -> None:
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": xh.numel() * 4,
                     "d2h_bytes_per_step": yh.numel() * 4, "steps": e2e_steps,
-                    "path": "k200_copy_async H2D + 2x k200_matmul + k200_copy_async D2H + k200_wait per step",
+                    "path": ("k200_copy_async H2D + 2x k200_matmul + k200_copy_async D2H + k200_wait per step"
+                             if world == 1 else
+                             "k200_copy_async H2D + 2x k200_matmul_q4_gather + k200_gather_wait + "
+                             "k200_copy_async D2H + k200_wait per step"),
                     "wall_s": t_wall},
             "gpu_launches": launches,
             "clocks": clock_info,
         }
+        if world > 1:
+            line["config"]["nvlink_bytes_per_step"] = 4 * (UP[1] + DOWN[1]) * (world - 1)
         print(json.dumps(line), flush=True)
     K.set_stream(dev, None)
     del g_main, g_rem
     if world > 1:
+        dist.barrier()  # no rank still uses another rank's exchange regions
+        ex_up.close()
+        ex_down.close()
         dist.barrier()
         dist.destroy_process_group()
 

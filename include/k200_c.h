@@ -218,6 +218,52 @@ int k200_swiglu(void *kernel, int device, void *y, size_t y_bytes, const void *g
                 const void *up, size_t up_bytes, int width, int rows, int gate_stride, int up_stride,
                 int output_stride, int type);
 
+/* ---- row-sharded batch-1 Q4_0 matmul with a fused all-gather over peer memory
+ * Replaces the gather of a row split: the reference's consumers split output
+ * rows over devices and move the slices with kunlun::peer copies
+ * (src/k200.cpp:89-95; "Row Split", docs/common-q4.md:23,31).  Here the GEMV
+ * of each rank stores its rows straight into every rank's output buffer over
+ * NVLink and then publishes a per-exchange epoch, so no separate collective
+ * runs.  One process per GPU; every rank maps the other ranks' buffers with
+ * k200_ipc_open.
+ *
+ * An exchange is, on every rank, one output buffer of the full N rows, one
+ * flag array of `ranks` words and two counter words, all zeroed before the
+ * first call.  k200_gather describes it from this rank: y[r] and flags[r] are
+ * rank r's buffer and flag array as addresses valid on this device (own
+ * allocations or IPC mappings); counter is this rank's own two words.  After
+ * k200_matmul_q4_gather, y[r] + row_begin .. + n on every rank holds this
+ * rank's rows; once every rank's call has finished, flags on every rank hold
+ * the same epoch for every rank.  wait_for (optional) names the exchange that
+ * produced x: the GEMV first waits, on the device, until every rank has
+ * published at least this rank's own epoch of it.  A wait that runs out
+ * (about a quarter of a second) posts 0x4b03 to the device's error word
+ * (k200_wait returns it) and the call completes without waiting further.
+ * Calls on one exchange must be issued in the same order on every rank, on
+ * one stream per rank.  A rank that reuses an output buffer while another
+ * rank may still read the previous contents races: alternate two buffers. */
+#define K200_GATHER_MAX_RANKS 8
+#define K200_GATHER_UNSUPPORTED (-4)
+typedef struct {
+    int ranks, rank;
+    float *y[K200_GATHER_MAX_RANKS];
+    unsigned *flags[K200_GATHER_MAX_RANKS];
+    unsigned *counter;
+} k200_gather;
+/* IPC of a device allocation's base address (64-byte handles). */
+int k200_ipc_handle(const void *device_ptr, void *handle);
+int k200_ipc_open(int device, const void *handle, void **device_ptr);
+int k200_ipc_close(int device, void *device_ptr);
+/* Zeroed scratch the GEMV needs for a shard of n rows (0: shape not handled). */
+size_t k200_matmul_q4_gather_scratch(int device, int k, int n);
+/* Y rows [row_begin, row_begin + n) = W . x for this rank's n rows of Q4_0
+ * weights W (batch 1, K % 256 == 0, 16-byte aligned W and x); scratch as
+ * above, left zeroed.  0, K200_GATHER_UNSUPPORTED or a CUDA error code. */
+int k200_matmul_q4_gather(int device, const k200_gather *out, int row_begin, const void *w, const void *x, int k,
+                          int n, void *scratch, size_t scratch_bytes, const k200_gather *wait_for);
+/* The wait alone (for the last exchange of a sequence). */
+int k200_gather_wait(int device, const k200_gather *exchange);
+
 #ifdef __cplusplus
 }
 #endif

@@ -62,6 +62,13 @@ _SIGNATURES = {
     "k200_set_stream": (None, [C.c_int, C.c_void_p]),
     "k200_set_static_weights": (None, [C.c_int, C.c_int]),
     "k200_quantize_q4_0": (None, [C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int]),
+    "k200_ipc_handle": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "k200_ipc_open": (C.c_int, [C.c_int, C.c_void_p, C.POINTER(C.c_void_p)]),
+    "k200_ipc_close": (C.c_int, [C.c_int, C.c_void_p]),
+    "k200_matmul_q4_gather_scratch": (C.c_size_t, [C.c_int, C.c_int, C.c_int]),
+    "k200_matmul_q4_gather": (C.c_int, [C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
+                                        C.c_void_p, C.c_size_t, C.c_void_p]),
+    "k200_gather_wait": (C.c_int, [C.c_int, C.c_void_p]),
     "k200_matmul_i8_noalloc": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
                                          C.c_void_p, C.c_void_p]),
     # native Q4 layout
@@ -704,3 +711,56 @@ def weight_bytes(type: int, k: int, n: int) -> int:
     if type == ROWWISE_I8:
         return packed_i8_size(k, n)
     raise ValueError(type)
+
+
+# ---------------------------------------------------------------------------
+# row-sharded batch-1 Q4_0 GEMV with a fused all-gather over peer memory
+# (k200_c.h; replaces the peer-copy gather of a row split, src/k200.cpp:89-95)
+# ---------------------------------------------------------------------------
+GATHER_MAX_RANKS, GATHER_UNSUPPORTED = 8, -4
+IPC_HANDLE_BYTES = 64
+
+
+class GatherView(C.Structure):
+    """k200_gather: one exchange seen from one rank (addresses valid on its device)."""
+    _fields_ = [("ranks", C.c_int), ("rank", C.c_int), ("y", C.c_void_p * GATHER_MAX_RANKS),
+                ("flags", C.c_void_p * GATHER_MAX_RANKS), ("counter", C.c_void_p)]
+
+
+def ipc_handle(ptr) -> bytes:
+    """64-byte CUDA IPC handle of a device allocation's base address."""
+    buf = C.create_string_buffer(IPC_HANDLE_BYTES)
+    check(lib().k200_ipc_handle(_ptr(ptr), buf))
+    return buf.raw
+
+
+def ipc_open(device: int, handle: bytes) -> int:
+    """Maps another process's allocation on `device`; returns its address here."""
+    out = C.c_void_p()
+    check(lib().k200_ipc_open(device, C.create_string_buffer(bytes(handle), IPC_HANDLE_BYTES), C.byref(out)))
+    return out.value
+
+
+def ipc_close(device: int, ptr) -> None:
+    check(lib().k200_ipc_close(device, _ptr(ptr)))
+
+
+def matmul_q4_gather_scratch(device: int, k: int, n: int) -> int:
+    """Zeroed scratch bytes k200_matmul_q4_gather needs for a shard of n rows (0: not handled)."""
+    return lib().k200_matmul_q4_gather_scratch(device, k, n)
+
+
+def matmul_q4_gather(device: int, out: GatherView, row_begin: int, w, x, k: int, n: int, scratch,
+                     scratch_bytes: int, wait_for: GatherView | None = None) -> int:
+    """This rank's rows of Y = W.x stored into every rank's output (k200_matmul_q4_gather).
+
+    Returns 0, GATHER_UNSUPPORTED or a CUDA error code; asynchronous on the library stream.
+    """
+    return lib().k200_matmul_q4_gather(device, C.addressof(out), row_begin, _ptr(w), _ptr(x), k, n, _ptr(scratch),
+                                       scratch_bytes, None if wait_for is None else C.addressof(wait_for))
+
+
+def gather_wait(device: int, exchange: GatherView) -> int:
+    """Device-side wait until every rank has published this rank's epoch of `exchange`."""
+    return lib().k200_gather_wait(device, C.addressof(exchange))
+

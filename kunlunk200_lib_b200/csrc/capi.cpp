@@ -5,6 +5,8 @@
 
 #include <cuda_runtime.h>
 
+#include <cstring>
+
 #include "k200_internal.h"
 
 namespace k200 {
@@ -15,7 +17,21 @@ size_t matmul_count(int device);
 bool common_q4_pack(const void *raw, size_t bytes, int k, int n, void *out, size_t out_bytes);
 size_t peer_copy_count();
 size_t peer_byte_count();
+int matmul_q4_gather(int device, const GatherLaunch &g, const void *w, const void *x, int k, int n, void *scratch,
+                     size_t scratch_bytes);
+int gather_wait(int device, const unsigned *flags, int ranks, int rank);
+size_t q4_gather_scratch(int device, int k, int n);
 }  // namespace k200
+
+namespace {
+bool gather_ok(const k200_gather *g) {
+    if (!g || g->ranks < 1 || g->ranks > K200_GATHER_MAX_RANKS || g->rank < 0 || g->rank >= g->ranks || !g->counter)
+        return false;
+    for (int r = 0; r < g->ranks; ++r)
+        if (!g->y[r] || !g->flags[r]) return false;
+    return true;
+}
+}  // namespace
 
 extern "C" {
 
@@ -115,6 +131,67 @@ int k200_matmul_i8_noalloc(int device, void *y, const void *w, const void *x, in
     static_assert(K200_NOALLOC_TOO_LARGE == k200::kNoAllocTooLarge, "k200_c.h status out of date");
     static_assert(K200_NOALLOC_NOT_READY == k200::kNoAllocNotReady, "k200_c.h status out of date");
     return k200::matmul_i8_noalloc(device, y, w, x, k, n, batch, scales, maxima);
+}
+
+// ---- row-sharded Q4_0 GEMV with a fused all-gather ---------------------------
+int k200_ipc_handle(const void *device_ptr, void *handle) {
+    kunlun::require(device_ptr && handle);
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void *>(device_ptr));
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return (int)e;
+    }
+    static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+    std::memcpy(handle, &h, sizeof(h));
+    return 0;
+}
+
+int k200_ipc_open(int device, const void *handle, void **device_ptr) {
+    std::lock_guard<std::recursive_mutex> lock(kunlun::runtime_mutex());
+    kunlun::require(handle && device_ptr);
+    kunlun::select(device);
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    const cudaError_t e = cudaIpcOpenMemHandle(device_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) cudaGetLastError();
+    return (int)e;
+}
+
+int k200_ipc_close(int device, void *device_ptr) {
+    std::lock_guard<std::recursive_mutex> lock(kunlun::runtime_mutex());
+    kunlun::require(device_ptr != nullptr);
+    kunlun::select(device);
+    const cudaError_t e = cudaIpcCloseMemHandle(device_ptr);
+    if (e != cudaSuccess) cudaGetLastError();
+    return (int)e;
+}
+
+size_t k200_matmul_q4_gather_scratch(int device, int k, int n) { return k200::q4_gather_scratch(device, k, n); }
+
+int k200_matmul_q4_gather(int device, const k200_gather *out, int row_begin, const void *w, const void *x, int k,
+                          int n, void *scratch, size_t scratch_bytes, const k200_gather *wait_for) {
+    static_assert(K200_GATHER_MAX_RANKS == k200::kGatherMaxRanks, "k200_c.h rank limit out of date");
+    kunlun::require(gather_ok(out) && (!wait_for || gather_ok(wait_for)) && row_begin >= 0 && n > 0);
+    k200::GatherLaunch g;
+    g.ranks = out->ranks;
+    g.rank = out->rank;
+    for (int r = 0; r < out->ranks; ++r) {
+        g.y[r] = out->y[r] + row_begin;
+        g.flags[r] = out->flags[r];
+    }
+    g.counter = out->counter;
+    if (wait_for) {
+        g.wait_flags = wait_for->flags[wait_for->rank];
+        g.wait_ranks = wait_for->ranks;
+        g.wait_rank = wait_for->rank;
+    }
+    return k200::matmul_q4_gather(device, g, w, x, k, n, scratch, scratch_bytes);
+}
+
+int k200_gather_wait(int device, const k200_gather *exchange) {
+    kunlun::require(gather_ok(exchange));
+    return k200::gather_wait(device, exchange->flags[exchange->rank], exchange->ranks, exchange->rank);
 }
 
 // ---- native Q4 layout ---------------------------------------------------------

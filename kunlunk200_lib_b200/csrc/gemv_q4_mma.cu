@@ -90,6 +90,7 @@ struct Q4MmaArgs {
     int k, n, tiles, ppr, grid, prefetch;
     int max_tiles;      // row tiles any CTA touches (partial-sum slots in shared memory)
     int max_boxes;      // boxes any CTA streams (entries of the box table)
+    GatherLaunch g;     // fused all-gather (g.ranks > 0) and the wait for X (g.wait_flags)
 };
 
 // Tensor maps over the weight rows viewed as 32-bit words [n][row_bytes/4],
@@ -242,12 +243,15 @@ __device__ __forceinline__ int cta_of(uint32_t u, uint32_t units, int grid) {
 // x[a1+1] and the same +16 (see lane_bytes); store_slot scales the block by
 // 2^-e so that its largest magnitude lies in [2^14, 2^15), splits the values
 // into f16 hi + lo and stores them (all 32 lanes of the warp must call it).
-__device__ __forceinline__ void load_slot(const float *xb, int p, int c, float (&v)[8]) {
+// (peer: X was written by other GPUs during this launch's lifetime; read it
+// through L2 rather than the read-only path)
+__device__ __forceinline__ void load_slot(const float *xb, int p, int c, float (&v)[8], bool peer) {
     const int a0 = pair_first(p, c), a1 = pair_second(p, c);
-    const float2 l0 = __ldg(reinterpret_cast<const float2 *>(xb + a0));
-    const float2 l1 = __ldg(reinterpret_cast<const float2 *>(xb + a1));
-    const float2 h0 = __ldg(reinterpret_cast<const float2 *>(xb + a0 + 16));
-    const float2 h1 = __ldg(reinterpret_cast<const float2 *>(xb + a1 + 16));
+    const float2 *q0 = reinterpret_cast<const float2 *>(xb + a0), *q1 = reinterpret_cast<const float2 *>(xb + a1);
+    const float2 l0 = peer ? __ldcg(q0) : __ldg(q0);
+    const float2 l1 = peer ? __ldcg(q1) : __ldg(q1);
+    const float2 h0 = peer ? __ldcg(q0 + 8) : __ldg(q0 + 8);
+    const float2 h1 = peer ? __ldcg(q1 + 8) : __ldg(q1 + 8);
     // register order = fragment order: {q0, q2}, {q0+16, q2+16}, {q1, q3}, {q1+16, q3+16}
     v[0] = l0.x; v[1] = l1.x; v[2] = h0.x; v[3] = h1.x;
     v[4] = l0.y; v[5] = l1.y; v[6] = h0.y; v[7] = h1.y;
@@ -304,6 +308,32 @@ __device__ __forceinline__ void st_relaxed(unsigned long long *p, unsigned long 
 }
 constexpr unsigned long long kPresent = 1ull << 32;
 constexpr uint32_t kPeerBudget = 1u << 20;   // polls of a partial sum (with 64 ns sleeps)
+
+// Flags of the fused all-gather live in every rank's memory and are written
+// by other GPUs: system-scope acquire loads and release stores.
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Waits until every rank's entry of this rank's flag array has reached this
+// rank's own entry (epochs only grow; compared modulo 2^32).  Single thread.
+__device__ __forceinline__ void wait_peer_flags(const unsigned *flags, int ranks, int rank, int *err) {
+    const unsigned target = ld_acquire_sys(flags + rank);
+    for (int r = 0; r < ranks; ++r) {
+        if (r == rank) continue;
+        for (uint32_t spin = 0; static_cast<int>(ld_acquire_sys(flags + r) - target) < 0; ++spin) {
+            if (spin >= kPeerBudget) {
+                atomicExch(err, kErrPeerTimeout);
+                break;
+            }
+            __nanosleep(256);
+        }
+    }
+}
 
 __global__ void __launch_bounds__(kThreads, 1)
     q4_mma_gemv_kernel(const __grid_constant__ Q4MmaMaps maps, const Q4MmaArgs a) {
@@ -363,6 +393,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // ---------------- consumers ----------------
     pdl_wait_prior();  // x, y and the partial-sum words may belong to the previous kernel
+    const bool peer_x = a.g.wait_flags != nullptr;
+    if (peer_x) {
+        // X is the output of another exchange: every rank must have stored its rows
+        if (tid == 0) wait_peer_flags(a.g.wait_flags, a.g.wait_ranks, a.g.wait_rank, a.err);
+        consumer_sync();
+    }
     {
         // fragment records: four threads per activation block; every load of a
         // thread is issued before the first conversion
@@ -373,7 +409,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int k = 0; k < kPasses; ++k)
             if (k * kWarps * 32 < nslots) {
                 const int b = min(k * kWarps * 32 + tid, nslots - 1) >> 2;
-                load_slot(a.x + 32 * b, b & 3, lane & 3, xv[k]);
+                load_slot(a.x + 32 * b, b & 3, lane & 3, xv[k], peer_x);
             }
 #pragma unroll
         for (int k = 0; k < kPasses; ++k)
@@ -447,7 +483,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         }
-        if (row < a.n) a.y[row] = v;
+        if (row < a.n) {
+            a.y[row] = v;
+            // fused all-gather: the same row into every other rank's output
+            for (int r = 0; r < a.g.ranks; ++r)
+                if (r != a.g.rank) a.g.y[r][row] = v;
+        }
     };
 
     // boxes of this CTA: the first segment, the full row tiles, the last segment
@@ -536,6 +577,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (cur >= 0) flush(cur);
     consumer_sync();  // every warp's partials are in shared memory
     for (int ts = warp; ts <= t_last - t_first; ts += kWarps) finish_tile(ts);
+    if (a.g.ranks > 0) {
+        // The last block of the launch to get here publishes the exchange's
+        // next epoch on every rank, after every block's row stores.
+        __threadfence_system();
+        consumer_sync();
+        if (tid == 0) {
+            __threadfence_system();
+            const unsigned arrived = atomicAdd(a.g.counter, 1u) + 1u;
+            if (arrived == static_cast<unsigned>(a.grid)) {
+                __threadfence_system();
+                a.g.counter[0] = 0u;  // the next launch's blocks arrive after this one completes
+                const unsigned epoch = a.g.counter[1] + 1u;
+                a.g.counter[1] = epoch;
+                for (int r = 0; r < a.g.ranks; ++r) st_release_sys(a.g.flags[r] + a.g.rank, epoch);
+            }
+        }
+    }
+}
+
+// Waits, in one thread, for an exchange's flags (launch_gather_wait).
+__global__ void gather_wait_kernel(const unsigned *flags, int ranks, int rank, int *err) {
+    pdl_wait_prior();
+    if (threadIdx.x == 0) wait_peer_flags(flags, ranks, rank, err);
 }
 
 struct Q4MmaPlan {
@@ -645,6 +709,7 @@ cudaError_t launch_q4_mma_gemv(const GemvRequest &r, const DeviceInfo &dev, cuda
     a.prefetch = r.prefetch_weights ? 1 << 30 : 0;
     a.max_tiles = p.max_tiles;
     a.max_boxes = p.max_boxes;
+    if (r.gather) a.g = *r.gather;
     static int configured[64] = {0};
     int devno = 0;
     cudaGetDevice(&devno);
@@ -665,6 +730,20 @@ cudaError_t launch_q4_mma_gemv(const GemvRequest &r, const DeviceInfo &dev, cuda
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, q4_mma_gemv_kernel, maps, a);
+}
+
+cudaError_t launch_gather_wait(const unsigned *flags, int ranks, int rank, const DeviceInfo &dev,
+                               cudaStream_t stream) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(32);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gather_wait_kernel, flags, ranks, rank, dev.err);
 }
 
 }  // namespace k200

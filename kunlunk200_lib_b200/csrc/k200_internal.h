@@ -14,6 +14,23 @@ struct DeviceInfo {
     int *err = nullptr;     // device view of the mapped error word
 };
 
+// Fused all-gather of a row-sharded batch-1 Q4_0 GEMV over peer memory
+// (k200_matmul_q4_gather): the rows this rank computes are stored into every
+// rank's output buffer, and the last block of the launch then publishes the
+// exchange's new epoch in every rank's flag array.  A launch can first wait
+// until every rank has published at least this rank's own epoch of another
+// exchange (the one that produced its X).
+constexpr int kGatherMaxRanks = 8;
+constexpr int kGatherUnsupported = -4;  // K200_GATHER_UNSUPPORTED
+struct GatherLaunch {
+    int ranks = 0, rank = 0;                    // ranks 0: no gather
+    float *y[kGatherMaxRanks] = {};             // every rank's output rows (offset to this shard)
+    unsigned *flags[kGatherMaxRanks] = {};      // every rank's flag array of the exchange
+    unsigned *counter = nullptr;                // this rank's {arrivals, epoch} words
+    const unsigned *wait_flags = nullptr;       // this rank's flag array of the exchange that made X
+    int wait_ranks = 0, wait_rank = 0;
+};
+
 // One legacy matmul launch: Y[c, r] = W[r, :] . X[c, :].
 struct GemvRequest {
     int wt;                        // 0 f32, 1 f16, 2 q4_0, 3 rowwise int8
@@ -33,6 +50,7 @@ struct GemvRequest {
     bool tensor_cores = true;      // batched shapes may take the tcgen05 GEMM (KUNLUN_TC=0: never)
     void *split = nullptr;         // Kernel-owned scratch for the GEMM's split activations
     size_t split_bytes = 0;        // (gemm_tc_scratch_bytes)
+    const GatherLaunch *gather = nullptr;  // batch-1 Q4_0 only (launch_q4_mma_gemv)
 };
 
 // Streaming GEMV launcher (handles any batch by column groups).
@@ -55,6 +73,10 @@ bool gemm_tc_supported(int wt, int k, int n, int batch);  // (q4_0 also needs k 
 size_t gemm_tc_scratch_bytes(int wt, int k, int n, int batch);
 cudaError_t launch_gemm_tc(const GemvRequest &r, const DeviceInfo &dev, cudaStream_t stream);
 cudaError_t launch_q4_mma_gemv(const GemvRequest &r, const DeviceInfo &dev, cudaStream_t stream);
+// One thread waits until every rank's flag in this rank's array of an
+// exchange has reached this rank's own (kErrPeerTimeout after its budget).
+cudaError_t launch_gather_wait(const unsigned *flags, int ranks, int rank, const DeviceInfo &dev,
+                               cudaStream_t stream);
 // Row gathers (get_rows.cu); an index outside [0, n) writes no output and
 // sets *status to 1 (else 0).
 cudaError_t launch_get_rows_f32(float *out, const float *in, const int32_t *idx, int *status, int k, int n, int rows,

@@ -588,6 +588,62 @@ void count_matmul(int device) {
 size_t peer_copy_count() { return kunlun::peer_copies.load(); }
 size_t peer_byte_count() { return kunlun::peer_bytes.load(); }
 
+size_t q4_gather_scratch(int id, int k, int n) {
+    using namespace kunlun;
+    std::lock_guard<std::recursive_mutex> lock(mutex);
+    require(id >= 0 && id < cuda_device_count());
+    if (k <= 0 || k > 16384 || k % 32 != 0 || n <= 0) return 0;
+    return q4_mma_scratch_bytes(k, n, 1, state(id).info);
+}
+
+// Batch-1 Q4_0 GEMV of this rank's rows with the fused all-gather
+// (k200_matmul_q4_gather).  Only the tensor-core GEMV stores rows to peers,
+// so a shape it does not take is declined, never run another way.
+int matmul_q4_gather(int id, const GatherLaunch &g, const void *w, const void *x, int k, int n, void *scratch,
+                     size_t scratch_bytes) {
+    using namespace kunlun;
+    std::lock_guard<std::recursive_mutex> lock(mutex);
+    require(id >= 0 && id < cuda_device_count());
+    require(k > 0 && k <= 16384 && k % 32 == 0 && n > 0 && w && x && scratch);
+    require(g.ranks >= 1 && g.ranks <= kGatherMaxRanks && g.rank >= 0 && g.rank < g.ranks && g.counter);
+    require(!g.wait_flags || (g.wait_ranks >= 1 && g.wait_ranks <= kGatherMaxRanks && g.wait_rank >= 0 &&
+                              g.wait_rank < g.wait_ranks));
+    select(id);
+    DeviceState &d = state(id);
+    const size_t need = q4_mma_scratch_bytes(k, n, 1, d.info);
+    if (!need || !d.q4_mma) return kGatherUnsupported;
+    require(scratch_bytes >= need);
+    GemvRequest r{};
+    r.wt = (int)WeightType::q4_0;
+    r.w = w;
+    r.x = static_cast<const float *>(x);
+    r.y = g.y[g.rank];
+    r.k = k;
+    r.n = n;
+    r.batch = 1;
+    r.x_stride = k;
+    r.y_stride = n;
+    r.prefetch_weights = d.static_weights;
+    r.fixup = scratch;
+    r.fixup_bytes = scratch_bytes;
+    r.gather = &g;
+    const cudaError_t e = launch_q4_mma_gemv(r, d.info, d.stream);
+    if (e == cudaErrorNotSupported) return kGatherUnsupported;
+    if (e != cudaSuccess) return (int)e;
+    ++d.matmuls;
+    return 0;
+}
+
+int gather_wait(int id, const unsigned *flags, int ranks, int rank) {
+    using namespace kunlun;
+    std::lock_guard<std::recursive_mutex> lock(mutex);
+    require(id >= 0 && id < cuda_device_count() && flags && ranks >= 1 && ranks <= kGatherMaxRanks && rank >= 0 &&
+            rank < ranks);
+    select(id);
+    DeviceState &d = state(id);
+    return (int)launch_gather_wait(flags, ranks, rank, d.info, d.stream);
+}
+
 // Rowwise-int8 matmul whose activation scratch is the module's static array
 // instead of the Kernel's grown buffer.  Same contract, kernels and results as
 // kunlun::matmul(..., rowwise_i8, ...).  Nothing here allocates: the size

@@ -48,3 +48,93 @@ def gather_rows(gathered, n: int, world: int, batch: int = 1):
     import numpy as np
 
     return np.concatenate(parts, axis=1)
+
+
+class PeerExchange:
+    """One all-gather exchange of a row-sharded batch-1 Q4_0 GEMV (k200_matmul_q4_gather).
+
+    Every rank owns one device region, zeroed at creation:
+      ``buffers`` output buffers of the full ``n`` rows (floats, each padded to
+      a multiple of 64), then the exchange's flag array (``world`` words,
+      padded to 64 bytes), then this rank's two counter words.
+    ``bases[r]`` is rank r's region as an address valid on this rank's device
+    (its own allocation, or an IPC mapping of the other rank's).  ``view(b)``
+    is the k200_gather of output buffer b; alternate buffers between
+    consecutive uses, so that a rank that runs ahead never overwrites rows
+    another rank is still reading.
+    """
+
+    def __init__(self, K, device: int, n: int, world: int, rank: int, bases: list[int], buffers: int = 2,
+                 owned=None, mapped=()):
+        if not 1 <= world <= K.GATHER_MAX_RANKS or not 0 <= rank < world or len(bases) != world:
+            raise ValueError(f"bad exchange: world={world} rank={rank} bases={len(bases)}")
+        self.K, self.device, self.n, self.world, self.rank, self.buffers = K, device, n, world, rank, buffers
+        self.n_pad = self.padded(n)
+        self._owned, self._mapped = owned, list(mapped)
+        flags_off = buffers * self.n_pad * 4
+        self.views = []
+        for b in range(buffers):
+            v = K.GatherView()
+            v.ranks, v.rank = world, rank
+            for r in range(world):
+                v.y[r] = bases[r] + b * self.n_pad * 4
+                v.flags[r] = bases[r] + flags_off
+            v.counter = bases[rank] + flags_off + 64
+            self.views.append(v)
+
+    @staticmethod
+    def padded(n: int) -> int:
+        return -(-n // 64) * 64
+
+    @classmethod
+    def region_bytes(cls, n: int, buffers: int = 2) -> int:
+        return buffers * cls.padded(n) * 4 + 128
+
+    @classmethod
+    def _region(cls, K, device: int, n: int, buffers: int):
+        import numpy as np
+
+        nbytes = cls.region_bytes(n, buffers)
+        buf = K.Buffer(device, nbytes)
+        buf.upload(np.zeros(nbytes, np.uint8))
+        return buf
+
+    @classmethod
+    def over_group(cls, K, device: int, n: int, world: int, rank: int, all_gather, buffers: int = 2):
+        """Collective: one region per rank, IPC handles swapped with ``all_gather(obj) -> list``."""
+        buf = cls._region(K, device, n, buffers)
+        handles = all_gather(K.ipc_handle(buf.data()))
+        bases, mapped = [], []
+        for r, h in enumerate(handles):
+            if r == rank:
+                bases.append(buf.data())
+            else:
+                p = K.ipc_open(device, h)
+                bases.append(p)
+                mapped.append(p)
+        return cls(K, device, n, world, rank, bases, buffers, owned=buf, mapped=mapped)
+
+    @classmethod
+    def on_one_device(cls, K, device: int, n: int, world: int, buffers: int = 2):
+        """All ranks' regions on one device, for running the ranks one after another in one stream."""
+        bufs = [cls._region(K, device, n, buffers) for _ in range(world)]
+        bases = [b.data() for b in bufs]
+        xs = [cls(K, device, n, world, r, bases, buffers) for r in range(world)]
+        xs[0]._owned = bufs  # the first rank's object keeps every region alive
+        return xs
+
+    def view(self, b: int):
+        return self.views[b % self.buffers]
+
+    def output(self, b: int) -> int:
+        """Address of this rank's own output buffer b (the full n rows)."""
+        return self.views[b % self.buffers].y[self.rank]
+
+    def close(self) -> None:
+        for p in self._mapped:
+            self.K.ipc_close(self.device, p)
+        self._mapped = []
+        owned = self._owned if isinstance(self._owned, list) else [self._owned] if self._owned else []
+        for b in owned:
+            b.close()
+        self._owned = None

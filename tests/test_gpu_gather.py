@@ -1,0 +1,155 @@
+"""Row-sharded batch-1 Q4_0 GEMV with the fused all-gather (k200_matmul_q4_gather).
+
+The reference's consumers split output rows over devices and gather the
+slices with kunlun::peer copies (src/k200.cpp:89-95, docs/common-q4.md:31);
+here each rank's GEMV stores its rows into every rank's output buffer and
+publishes an epoch.  Checks:
+  * ranks run one after another on one GPU (every wait is already satisfied
+    when it starts, so no kernel waits on one that has not run): every rank's
+    buffer holds every shard, bit-identical to k200_matmul on that shard, and
+    a chained second GEMV that waits for the first exchange reads the full
+    vector; flags carry one epoch per exchange use;
+  * a wait that nothing satisfies runs out and posts the peer-timeout status
+    (0x4b03) instead of hanging, and the device stays usable;
+  * on two GPUs (when present), the same chain across two processes.
+Bar: bit-exact against k200_matmul on the same shard (same kernel, same
+shape, so the same arithmetic).
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+from kunlunk200_lib_b200.shard import PeerExchange, row_shard
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PEER_TIMEOUT = 0x4B03
+
+
+def _q4(O, k, n, seed):
+    return O.q4_0_quantize(O.normal(seed, n * k, 0.0, 0.02), n, k)
+
+
+def _plain(K, dw, dx, k, n, row_begin, x_offset=0):
+    """Rows [row_begin, row_begin + n) through k200_matmul."""
+    row_bytes = k // 32 * 18
+    dy = K.Buffer(0, 4 * n)
+    kern = K.Kernel()
+    K.matmul(kern, 0, dy, dw.data() + row_begin * row_bytes, dx + x_offset, k, n, 1, K.Q4_0)
+    K.select(0)
+    K.check(K.wait())
+    y = dy.download(np.float32, n)
+    kern.close()
+    dy.close()
+    return y
+
+
+def _download(K, ptr, n):
+    out = np.empty(n, np.float32)
+    K.select(0)
+    K.check(K.copy(out, ptr, out.nbytes, K.DEVICE_TO_HOST))
+    return out
+
+
+def _flags(K, ex, world):
+    out = np.empty(world, np.uint32)
+    K.select(0)
+    K.check(K.copy(out, ex.view(0).flags[ex.rank], out.nbytes, K.DEVICE_TO_HOST))
+    return out
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_gather_ranks_on_one_gpu(K, O, gpu, world):
+    # the second GEMV reads 2048 values of the gathered 2000-row output: its
+    # rows plus the zeroed padding of the 2048-float buffer
+    k1, n1 = 4096, 2000
+    k2, n2 = 2048, 1024
+    q_up = _q4(O, k1, n1, 0x7340D123)
+    q_dn = _q4(O, k2, n2, 0x1234567)
+    x = O.uniform(0x09200ABC, k1, -1.0, 1.0)
+    dw1, dw2, dx = K.Buffer(0, q_up.nbytes), K.Buffer(0, q_dn.nbytes), K.Buffer(0, x.nbytes)
+    dw1.upload(q_up)
+    dw2.upload(q_dn)
+    dx.upload(x)
+    up = PeerExchange.on_one_device(K, 0, n1, world)
+    dn = PeerExchange.on_one_device(K, 0, n2, world)
+    rb1 = k1 // 32 * 18
+    rb2 = k2 // 32 * 18
+    scratch = max(K.matmul_q4_gather_scratch(0, k1, row_shard(n1, world, r)[1]) for r in range(world))
+    scratch = max([scratch] + [K.matmul_q4_gather_scratch(0, k2, row_shard(n2, world, r)[1]) for r in range(world)])
+    assert scratch > 0
+    sbuf = K.Buffer(0, scratch)
+    sbuf.upload(np.zeros(scratch, np.uint8))
+    for step in range(2):  # buffer 0, then buffer 1: epochs 1 and 2
+        for r in range(world):
+            b, c = row_shard(n1, world, r)
+            assert K.matmul_q4_gather(0, up[r].view(step), b, dw1.data() + b * rb1, dx.data(), k1, c,
+                                      sbuf.data(), scratch) == 0
+        for r in range(world):
+            b, c = row_shard(n2, world, r)
+            # x of the second GEMV: the first 2048 rows of this rank's gathered up output
+            assert K.matmul_q4_gather(0, dn[r].view(step), b, dw2.data() + b * rb2, up[r].output(step), k2, c,
+                                      sbuf.data(), scratch, wait_for=up[r].view(step)) == 0
+        K.select(0)
+        assert K.wait() == 0
+        full_up = np.concatenate([_plain(K, dw1, dx.data(), k1, row_shard(n1, world, r)[1], row_shard(n1, world, r)[0])
+                                  for r in range(world)])
+        for r in range(world):
+            got = _download(K, up[r].output(step), n1)
+            assert np.array_equal(got.view(np.uint32), full_up.view(np.uint32)), f"rank {r} up rows"
+            assert (_flags(K, up[r], world) == step + 1).all()
+            assert (_flags(K, dn[r], world) == step + 1).all()
+        xin = up[0].output(step)
+        full_dn = np.concatenate([_plain(K, dw2, xin, k2, row_shard(n2, world, r)[1], row_shard(n2, world, r)[0])
+                                  for r in range(world)])
+        for r in range(world):
+            got = _download(K, dn[r].output(step), n2)
+            assert np.array_equal(got.view(np.uint32), full_dn.view(np.uint32)), f"rank {r} down rows"
+    for xs in (up, dn):
+        for e in reversed(xs):
+            e.close()
+
+
+def test_gather_wait_runs_out(K, gpu):
+    """A flag that no rank sets: the device-side wait gives up with the peer-timeout status."""
+    ex = PeerExchange.on_one_device(K, 0, 64, 2)
+    own = np.array([1], np.uint32)  # rank 0 claims epoch 1; rank 1 never publishes it
+    K.select(0)
+    K.check(K.copy(ex[0].view(0).flags[0], own, 4, K.HOST_TO_DEVICE))
+    assert K.gather_wait(0, ex[0].view(0)) == 0
+    K.select(0)
+    assert K.wait() == PEER_TIMEOUT
+    # the context is still usable: a satisfied wait completes cleanly
+    assert K.gather_wait(0, ex[1].view(0)) == 0
+    assert K.wait() == 0
+    for e in reversed(ex):
+        e.close()
+
+
+def test_gather_declines_unsupported_shapes(K, gpu):
+    """Only the tensor-core batch-1 GEMV stores rows to peers; other shapes are declined, not rerouted."""
+    assert K.matmul_q4_gather_scratch(0, 4096 + 32, 100) == 0  # K % 256 != 0
+    ex = PeerExchange.on_one_device(K, 0, 128, 1)
+    dw, dx, s = K.Buffer(0, 128 * 130 * 18), K.Buffer(0, 4 * 4160), K.Buffer(0, 4096)
+    assert K.matmul_q4_gather(0, ex[0].view(0), 0, dw, dx, 4160, 128, s, 4096) == K.GATHER_UNSUPPORTED
+    ex[0].close()
+
+
+def test_gather_two_gpus(K, gpu):
+    """The chain over two processes, one per GPU, with IPC-mapped peer buffers."""
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", "--master-port=29561", os.path.join(ROOT, "tests", "gather_worker.py")]
+    p = subprocess.run(["timeout", "-k", "30", "240"] + cmd, cwd=ROOT, env=env, capture_output=True, text=True)
+    assert p.returncode == 0, p.stdout[-3000:] + p.stderr[-3000:]
+    assert p.stdout.count("gather worker ok") == 2, p.stdout[-2000:]

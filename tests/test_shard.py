@@ -84,3 +84,86 @@ def test_sharded_q4_gemv_matches_unsharded(O, n, batch):
         p.join(timeout=120)
         assert p.exitcode == 0
     assert np.array_equal(got, full)
+
+
+class _FakeK:
+    """Stand-in for the library's IPC and allocation calls (no GPU)."""
+    GATHER_MAX_RANKS = 8
+
+    def __init__(self):
+        from kunlunk200_lib_b200 import GatherView
+
+        self.GatherView = GatherView
+        self.opened, self.closed = [], []
+
+    def ipc_handle(self, ptr):
+        return ptr.to_bytes(8, "little") * 8
+
+    def ipc_open(self, device, handle):
+        p = int.from_bytes(handle[:8], "little") + 0x1000000  # "mapped" elsewhere
+        self.opened.append(p)
+        return p
+
+    def ipc_close(self, device, ptr):
+        self.closed.append(ptr)
+
+
+def _ranks_over_gloo(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from kunlunk200_lib_b200.shard import PeerExchange
+
+    class Buf:
+        def __init__(self, base):
+            self.base = base
+
+        def data(self):
+            return self.base
+
+        def close(self):
+            pass
+
+    K = _FakeK()
+    PeerExchange._region = classmethod(lambda cls, K_, dev, n, buffers: Buf(0x10000 * (rank + 1)))
+
+    def all_gather(obj):
+        got = [None] * world
+        dist.all_gather_object(got, obj)
+        return got
+
+    ex = PeerExchange.over_group(K, 0, 1000, world, rank, all_gather)
+    v0, v1 = ex.view(0), ex.view(1)
+    out.put((rank, [v0.y[r] for r in range(world)], [v1.y[r] for r in range(world)],
+             [v0.flags[r] for r in range(world)], v0.counter, ex.output(1), list(K.opened)))
+    ex.close()
+    assert sorted(K.closed) == sorted(K.opened)
+    dist.destroy_process_group()
+
+
+def test_peer_exchange_views_over_gloo():
+    """Each rank sees its own region directly and the others through their IPC handles."""
+    from kunlunk200_lib_b200.shard import PeerExchange
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    procs = [ctx.Process(target=_ranks_over_gloo, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(60)
+        assert p.exitcode == 0
+    pad = PeerExchange.padded(1000) * 4
+    assert pad == 1024 * 4
+    for rank, y0, y1, flags, counter, out1, opened in res:
+        for r in range(world):
+            base = 0x10000 * (r + 1) + (0 if r == rank else 0x1000000)
+            assert y0[r] == base and y1[r] == base + pad
+            assert flags[r] == base + 2 * pad
+        own = 0x10000 * (rank + 1)
+        assert counter == own + 2 * pad + 64 and out1 == own + pad
+        assert len(opened) == world - 1
