@@ -90,7 +90,6 @@ struct Q4MmaArgs {
     int k, n, tiles, ppr, grid, prefetch;
     int max_tiles;      // row tiles any CTA touches (partial-sum slots in shared memory)
     int max_boxes;      // boxes any CTA streams (entries of the box table)
-    GatherLaunch g;     // fused all-gather (g.ranks > 0) and the wait for X (g.wait_flags)
 };
 
 // Tensor maps over the weight rows viewed as 32-bit words [n][row_bytes/4],
@@ -335,8 +334,12 @@ __device__ __forceinline__ void wait_peer_flags(const unsigned *flags, int ranks
     }
 }
 
+// kGather: the fused all-gather (xg.ranks > 0) and the wait for X
+// (xg.wait_flags), in a separate instantiation with its own parameter, so that
+// the plain GEMV carries none of its code or registers.
+template <bool kGather>
 __global__ void __launch_bounds__(kThreads, 1)
-    q4_mma_gemv_kernel(const __grid_constant__ Q4MmaMaps maps, const Q4MmaArgs a) {
+    q4_mma_gemv_kernel(const __grid_constant__ Q4MmaMaps maps, const Q4MmaArgs a, const GatherLaunch xg) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int groups = a.k >> 7;
     uint8_t *ring = smem;
@@ -393,10 +396,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // ---------------- consumers ----------------
     pdl_wait_prior();  // x, y and the partial-sum words may belong to the previous kernel
-    const bool peer_x = a.g.wait_flags != nullptr;
+    const bool peer_x = kGather && xg.wait_flags != nullptr;
     if (peer_x) {
         // X is the output of another exchange: every rank must have stored its rows
-        if (tid == 0) wait_peer_flags(a.g.wait_flags, a.g.wait_ranks, a.g.wait_rank, a.err);
+        if (tid == 0) wait_peer_flags(xg.wait_flags, xg.wait_ranks, xg.wait_rank, a.err);
         consumer_sync();
     }
     {
@@ -486,8 +489,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (row < a.n) {
             a.y[row] = v;
             // fused all-gather: the same row into every other rank's output
-            for (int r = 0; r < a.g.ranks; ++r)
-                if (r != a.g.rank) a.g.y[r][row] = v;
+            if (kGather)
+                for (int r = 0; r < xg.ranks; ++r)
+                    if (r != xg.rank) xg.y[r][row] = v;
         }
     };
 
@@ -577,20 +581,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (cur >= 0) flush(cur);
     consumer_sync();  // every warp's partials are in shared memory
     for (int ts = warp; ts <= t_last - t_first; ts += kWarps) finish_tile(ts);
-    if (a.g.ranks > 0) {
+    if (kGather && xg.ranks > 0) {
         // The last block of the launch to get here publishes the exchange's
         // next epoch on every rank, after every block's row stores.
         __threadfence_system();
         consumer_sync();
         if (tid == 0) {
             __threadfence_system();
-            const unsigned arrived = atomicAdd(a.g.counter, 1u) + 1u;
+            const unsigned arrived = atomicAdd(xg.counter, 1u) + 1u;
             if (arrived == static_cast<unsigned>(a.grid)) {
                 __threadfence_system();
-                a.g.counter[0] = 0u;  // the next launch's blocks arrive after this one completes
-                const unsigned epoch = a.g.counter[1] + 1u;
-                a.g.counter[1] = epoch;
-                for (int r = 0; r < a.g.ranks; ++r) st_release_sys(a.g.flags[r] + a.g.rank, epoch);
+                xg.counter[0] = 0u;  // the next launch's blocks arrive after this one completes
+                const unsigned epoch = xg.counter[1] + 1u;
+                xg.counter[1] = epoch;
+                for (int r = 0; r < xg.ranks; ++r) st_release_sys(xg.flags[r] + xg.rank, epoch);
             }
         }
     }
@@ -709,15 +713,18 @@ cudaError_t launch_q4_mma_gemv(const GemvRequest &r, const DeviceInfo &dev, cuda
     a.prefetch = r.prefetch_weights ? 1 << 30 : 0;
     a.max_tiles = p.max_tiles;
     a.max_boxes = p.max_boxes;
-    if (r.gather) a.g = *r.gather;
-    static int configured[64] = {0};
+    const bool gather = r.gather != nullptr;
+    void (*kernel)(const Q4MmaMaps, const Q4MmaArgs, const GatherLaunch) =
+        gather ? q4_mma_gemv_kernel<true> : q4_mma_gemv_kernel<false>;
+    const GatherLaunch xg = gather ? *r.gather : GatherLaunch{};
+    static int configured[2][64] = {};
     int devno = 0;
     cudaGetDevice(&devno);
-    if (devno < 0 || devno >= 64 || configured[devno] < static_cast<int>(p.smem)) {
-        cudaError_t e = cudaFuncSetAttribute(q4_mma_gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (devno < 0 || devno >= 64 || configured[gather][devno] < static_cast<int>(p.smem)) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(p.smem));
         if (e != cudaSuccess) return e;
-        if (devno >= 0 && devno < 64) configured[devno] = static_cast<int>(p.smem);
+        if (devno >= 0 && devno < 64) configured[gather][devno] = static_cast<int>(p.smem);
     }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(p.grid);
@@ -729,7 +736,7 @@ cudaError_t launch_q4_mma_gemv(const GemvRequest &r, const DeviceInfo &dev, cuda
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, q4_mma_gemv_kernel, maps, a);
+    return cudaLaunchKernelEx(&cfg, kernel, maps, a, xg);
 }
 
 cudaError_t launch_gather_wait(const unsigned *flags, int ranks, int rank, const DeviceInfo &dev,
