@@ -314,7 +314,11 @@ def run_ours(args) -> None:
                             K.matmul_q4_gather_scratch(dev, DOWN[0], n_down))
         if not scratch_bytes:
             raise SystemExit("shard shape not handled by the batch-1 tensor-core GEMV")
-        scratch = torch.zeros(scratch_bytes, dtype=torch.uint8, device="cuda")
+        with torch.cuda.stream(stream):  # zeroed before the first GEMV on the library stream reads it
+            scratch = torch.zeros(scratch_bytes, dtype=torch.uint8, device="cuda")
+        stream.synchronize()
+        dist.barrier()  # every rank's regions are mapped and zeroed before any rank stores into them
+        torch.cuda.synchronize()
 
     def gemv_up(s: int):
         wu = weights[s % sets][0]
