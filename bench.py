@@ -357,6 +357,7 @@ def run_ours(args) -> None:
     K.check(K.wait())
     if world > 1:
         dist.barrier()  # the next sequence starts again at buffer 0
+        torch.cuda.synchronize()
 
     # one CUDA graph holds a whole number of rotations; the timed region
     # replays it until exactly `steps` steps ran (a remainder graph if needed)
@@ -415,6 +416,9 @@ def run_ours(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
     clock_info = clocks.stop() if rank == 0 else None
+    if world > 1:  # rank 0's host was busy with the clock record: start the next phase together
+        dist.barrier()
+        torch.cuda.synchronize()
     value = total_bytes * args.steps / (ms * 1e-3) / 1e9
     launches = args.steps * 2 + (reps + (1 if rem else 0)) * (world > 1)
 
@@ -713,6 +717,9 @@ def run_gemm(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
     clock_info = clocks.stop() if rank == 0 else None
+    if world > 1:  # rank 0's host was busy with the clock record: start the next phase together
+        dist.barrier()
+        torch.cuda.synchronize()
     flops_step = 2.0 * n * k * batch
     value = flops_step * args.steps / (ms * 1e-3) / 1e12
     ms_step = ms / args.steps

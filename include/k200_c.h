@@ -237,7 +237,7 @@ int k200_swiglu(void *kernel, int device, void *y, size_t y_bytes, const void *g
  * the same epoch for every rank.  wait_for (optional) names the exchange that
  * produced x: the GEMV first waits, on the device, until every rank has
  * published at least this rank's own epoch of it.  A wait that runs out
- * (about a quarter of a second) posts 0x4b03 to the device's error word
+ * (several seconds) posts 0x4b03 to the device's error word
  * (k200_wait returns it) and the call completes without waiting further.
  * Calls on one exchange must be issued in the same order on every rank, on
  * one stream per rank.  A rank that reuses an output buffer while another

@@ -318,6 +318,10 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
 __device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+// Polls of another rank's flag, with 1 us sleeps: several seconds, because
+// ranks are separate processes whose hosts can fall behind one another
+// (a pause in one process) while the other rank's GPU already waits.
+constexpr uint32_t kFlagBudget = 1u << 22;
 // Waits until every rank's entry of this rank's flag array has reached this
 // rank's own entry (epochs only grow; compared modulo 2^32).  Single thread.
 __device__ __forceinline__ void wait_peer_flags(const unsigned *flags, int ranks, int rank, int *err) {
@@ -325,11 +329,11 @@ __device__ __forceinline__ void wait_peer_flags(const unsigned *flags, int ranks
     for (int r = 0; r < ranks; ++r) {
         if (r == rank) continue;
         for (uint32_t spin = 0; static_cast<int>(ld_acquire_sys(flags + r) - target) < 0; ++spin) {
-            if (spin >= kPeerBudget) {
+            if (spin >= kFlagBudget) {
                 atomicExch(err, kErrPeerTimeout);
                 break;
             }
-            __nanosleep(256);
+            __nanosleep(1000);
         }
     }
 }
@@ -583,8 +587,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int ts = warp; ts <= t_last - t_first; ts += kWarps) finish_tile(ts);
     if (kGather && xg.ranks > 0) {
         // The last block of the launch to get here publishes the exchange's
-        // next epoch on every rank, after every block's row stores.
-        __threadfence_system();
+        // next epoch on every rank, after every block's row stores: the
+        // barrier orders this block's stores before thread 0's system-scope
+        // fence, which orders them before its arrival (one fence per block;
+        // a fence in every thread costs microseconds each).
         consumer_sync();
         if (tid == 0) {
             __threadfence_system();
