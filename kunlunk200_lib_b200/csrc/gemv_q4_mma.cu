@@ -318,10 +318,11 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
 __device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-// Polls of another rank's flag, with 1 us sleeps: several seconds, because
-// ranks are separate processes whose hosts can fall behind one another
-// (a pause in one process) while the other rank's GPU already waits.
-constexpr uint32_t kFlagBudget = 1u << 22;
+// Polls of another rank's flag, with short sleeps (a flag that arrives is
+// seen within a fraction of a microsecond): several seconds in all, because
+// ranks are separate processes whose hosts can fall behind one another (a
+// pause in one process) while the other rank's GPU already waits.
+constexpr uint32_t kFlagBudget = 1u << 23;
 // Waits until every rank's entry of this rank's flag array has reached this
 // rank's own entry (epochs only grow; compared modulo 2^32).  Single thread.
 __device__ __forceinline__ void wait_peer_flags(const unsigned *flags, int ranks, int rank, int *err) {
@@ -333,7 +334,7 @@ __device__ __forceinline__ void wait_peer_flags(const unsigned *flags, int ranks
                 atomicExch(err, kErrPeerTimeout);
                 break;
             }
-            __nanosleep(1000);
+            __nanosleep(200);
         }
     }
 }
