@@ -139,6 +139,12 @@ def test_reference_consumers_link_against_this_library():
         assert wanted and wanted <= exported, sorted(wanted - exported)
 
 
+# a well-formed two-rank exchange view (dummy addresses) that each case then breaks
+_GATHER = ("v = K.GatherView()\nv.ranks, v.rank = 2, 0\n"
+           "for r in range(2):\n    v.y[r] = 4096 * (r + 1)\n    v.flags[r] = 65536 * (r + 1)\n"
+           "v.counter = 1 << 20\n")
+
+
 def _run_contract(snippet: str) -> subprocess.CompletedProcess:
     code = (
         "import sys; sys.path.insert(0, %r)\n"
@@ -162,6 +168,13 @@ def _run_contract(snippet: str) -> subprocess.CompletedProcess:
         ("elementwise width", "K.elementwise(kern, 0, 16, 16, 16, 100, 33, 100, K.ADD)"),
         ("rms epsilon", "K.elementwise(kern, 0, 16, 16, 16, 64, 32, 64, K.RMS_NORM, 0.0)"),
         ("i8 upload bounds", "K.upload_i8_rows(0, 16, 32, 4, 3, 2, 16)"),
+        ("gather without ranks", _GATHER + "v.ranks = 0\nK.matmul_q4_gather(0, v, 0, 16, 16, 4096, 16, 16, 64)"),
+        ("gather rank out of range", _GATHER + "v.rank = 2\nK.matmul_q4_gather(0, v, 0, 16, 16, 4096, 16, 16, 64)"),
+        ("gather null peer output", _GATHER + "v.y[1] = None\nK.matmul_q4_gather(0, v, 0, 16, 16, 4096, 16, 16, 64)"),
+        ("gather wait on a bad exchange", _GATHER + "w = K.GatherView()\n"
+                                          "K.matmul_q4_gather(0, v, 0, 16, 16, 4096, 16, 16, 64, wait_for=w)"),
+        ("gather negative first row", _GATHER + "K.matmul_q4_gather(0, v, -16, 16, 16, 4096, 16, 16, 64)"),
+        ("gather wait without ranks", _GATHER + "v.ranks = 0\nK.gather_wait(0, v)"),
     ],
 )
 def test_contract_violations_abort(case, call):
