@@ -479,6 +479,12 @@ def run_ours(args) -> None:
 
     cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
 
+    # the committed capture is of full-size launches; a shard's launch streams
+    # its rows' share of the weights (traffic tracks the algorithmic bytes)
+    shard_traffic = profile_traffic("q4_mma_gemv_k4096_n11008.md")
+    if shard_traffic is not None and world > 1:
+        full_alg = q4_bytes(*UP) + 4 * UP[0] + 4 * UP[1]
+        shard_traffic = int(shard_traffic * ((alg_up + alg_down) / 2) / full_alg)
     if rank == 0:
         line = {
             "metric": "q4_0_gemv_weight_gbps", "value": value, "unit": "GB/s", "n_gpus": world,
@@ -496,7 +502,7 @@ def run_ours(args) -> None:
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / peaks["hbm_gbs"],
                          "peak_source": peaks["source"],
-                         "traffic": profile_traffic("q4_mma_gemv_k4096_n11008.md"),
+                         "traffic": shard_traffic,
                          "kernel": "q4_mma_gemv_kernel",
                          "launch_us": launch_ms * 1e3,
                          "isolated_launch_us": {"up": mean_up * 1e3, "down": mean_down * 1e3},
