@@ -652,15 +652,18 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// Tensor maps of a weight matrix, cached by (pointer, k, n).  Called with the
-// library's runtime mutex held.
+// Tensor maps of a weight matrix, cached by (pointer, k, n): enough entries
+// for the weights a serving loop or a sharded bench rotates through, so that
+// the maps are encoded once per weight.  Called with the library's runtime
+// mutex held.
+constexpr int kMapCache = 128;
 bool weight_maps(Q4MmaMaps &out, const void *w, int k, int n) {
     struct Entry {
         const void *w = nullptr;
         int k = 0, n = 0;
         Q4MmaMaps maps;
     };
-    static Entry cache[16];
+    static Entry cache[kMapCache];
     static int next = 0;
     for (const Entry &e : cache)
         if (e.w == w && e.k == k && e.n == n) {
@@ -685,7 +688,7 @@ bool weight_maps(Q4MmaMaps &out, const void *w, int k, int n) {
     cache[next].k = k;
     cache[next].n = n;
     cache[next].maps = maps;
-    next = (next + 1) % 16;
+    next = (next + 1) % kMapCache;
     out = maps;
     return true;
 }
