@@ -103,14 +103,19 @@ void k200_pack_i8_rows_device(int device, void *weights, int k, int rows, int fi
  * one fixed array per device in the library's device image, so:
  *   - batch*k must be <= K200_NOALLOC_MAX_ELEMENTS; larger calls return
  *     K200_NOALLOC_TOO_LARGE (with a message on stderr) and do nothing;
- *   - the device must already be set up by k200_select(device) (which creates
- *     its stream and error word), else K200_NOALLOC_NOT_READY;
+ *   - the device must already be set up by k200_select(device), else
+ *     K200_NOALLOC_NOT_READY.  That first select on a device is where the
+ *     array's memory is taken: it creates the device's stream and error word
+ *     and loads the module holding the array (CUDA loads modules lazily), so
+ *     a caller that hands the rest of the device to its own pool should
+ *     select the device before doing so;
  *   - overlapping calls on one device race on that array: calls issued on the
  *     same stream are ordered, but calls whose work can run concurrently
  *     (issued on different streams, see k200_set_stream) are not, and must be
  *     serialised by the caller.  (Each process has its own copy.)
  * Arguments, packing and results are those of k200_matmul with type 3
- * (rowwise_i8); results are bit-identical.  Returns 0 once the work is
+ * (rowwise_i8); results are bit-identical, and the same kernels run (the
+ * tcgen05 int8 GEMM from batch 4, unless KUNLUN_TC=0).  Returns 0 once the work is
  * submitted (completion via k200_select + k200_wait), a K200_NOALLOC_* status,
  * or a CUDA error code.  Contract violations abort as in k200_matmul. */
 #define K200_NOALLOC_MAX_ELEMENTS 2097152
@@ -249,6 +254,7 @@ typedef struct {
     float *y[K200_GATHER_MAX_RANKS];
     unsigned *flags[K200_GATHER_MAX_RANKS];
     unsigned *counter;
+    int rows; /* rows of every rank's output buffer: row_begin + n must not exceed it */
 } k200_gather;
 /* IPC of a device allocation's base address (64-byte handles). */
 int k200_ipc_handle(const void *device_ptr, void *handle);

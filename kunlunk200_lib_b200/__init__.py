@@ -724,7 +724,8 @@ IPC_HANDLE_BYTES = 64
 class GatherView(C.Structure):
     """k200_gather: one exchange seen from one rank (addresses valid on its device)."""
     _fields_ = [("ranks", C.c_int), ("rank", C.c_int), ("y", C.c_void_p * GATHER_MAX_RANKS),
-                ("flags", C.c_void_p * GATHER_MAX_RANKS), ("counter", C.c_void_p)]
+                ("flags", C.c_void_p * GATHER_MAX_RANKS), ("counter", C.c_void_p),
+                ("rows", C.c_int)]
 
 
 def ipc_handle(ptr) -> bytes:

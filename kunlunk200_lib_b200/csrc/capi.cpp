@@ -25,7 +25,8 @@ size_t q4_gather_scratch(int device, int k, int n);
 
 namespace {
 bool gather_ok(const k200_gather *g) {
-    if (!g || g->ranks < 1 || g->ranks > K200_GATHER_MAX_RANKS || g->rank < 0 || g->rank >= g->ranks || !g->counter)
+    if (!g || g->ranks < 1 || g->ranks > K200_GATHER_MAX_RANKS || g->rank < 0 || g->rank >= g->ranks || !g->counter ||
+        g->rows < 1)
         return false;
     for (int r = 0; r < g->ranks; ++r)
         if (!g->y[r] || !g->flags[r]) return false;
@@ -173,6 +174,8 @@ int k200_matmul_q4_gather(int device, const k200_gather *out, int row_begin, con
                           int n, void *scratch, size_t scratch_bytes, const k200_gather *wait_for) {
     static_assert(K200_GATHER_MAX_RANKS == k200::kGatherMaxRanks, "k200_c.h rank limit out of date");
     kunlun::require(gather_ok(out) && (!wait_for || gather_ok(wait_for)) && row_begin >= 0 && n > 0);
+    // the rows are stored into every rank's buffer, over NVLink for the others
+    kunlun::require(n <= out->rows && row_begin <= out->rows - n);
     k200::GatherLaunch g;
     g.ranks = out->ranks;
     g.rank = out->rank;

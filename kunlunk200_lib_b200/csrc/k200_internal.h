@@ -83,11 +83,15 @@ cudaError_t launch_get_rows_f32(float *out, const float *in, const int32_t *idx,
                                 cudaStream_t stream);
 cudaError_t launch_common_get_rows(float *out, const uint8_t *w, size_t scale_offset, int kp, int np,
                                    const int32_t *idx, int *status, int k, int n, int rows, cudaStream_t stream);
-// Q6_K typed GEMV (q6_k.cu): chunk-256 A8 of one activation row, then the
-// int8 x int8 GEMV over the packed weights (n % 32 == 0, k % 256 == 0).
-cudaError_t launch_q6_quant(const void *x, int dtype, int k, int8_t *q, float *scales, cudaStream_t stream);
+// Q6_K typed GEMV (q6_k.cu), n % 32 == 0, k % 256 == 0: raw GGML blocks
+// [n][k/256][210 B] -> packed int8 values and f32 group scales (a non-finite
+// block scale sets *status); chunk-256 A8 of m activation rows ([m][k] int8,
+// [m][k/256] scales); then the int8 x int8 GEMV of those m rows.
+cudaError_t launch_q6_unpack(const uint8_t *raw, int k, int n, int8_t *w, float *wscale, int *status,
+                             cudaStream_t stream);
+cudaError_t launch_q6_quant(const void *x, int dtype, int k, int m, int8_t *q, float *scales, cudaStream_t stream);
 cudaError_t launch_q6_gemv(float *y, const int8_t *w, const float *wscale, const int8_t *q, const float *ascale, int k,
-                           int n, const DeviceInfo &dev, cudaStream_t stream);
+                           int n, int m, const DeviceInfo &dev, cudaStream_t stream);
 // kunlun::swiglu (swiglu.cu): y = SiLU(gate) * up, strides in bytes, f16 != 0: F16 rows.
 cudaError_t launch_swiglu(void *y, const void *gate, const void *up, int width, int rows, int gs, int us, int ys,
                           int f16, const DeviceInfo &dev, cudaStream_t stream);

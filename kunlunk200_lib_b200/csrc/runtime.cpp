@@ -109,6 +109,12 @@ DeviceState &state(int id) {
         fail_cuda(cudaDeviceGetAttribute(&d.info.sm_count, cudaDevAttrMultiProcessorCount, id), "sm count");
         fail_cuda(cudaDeviceGetAttribute(&d.info.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, id),
                   "smem opt-in");
+        // The static scratch of k200_matmul_i8_noalloc lives in a module that
+        // CUDA loads lazily, on first use.  Looking its address up here makes
+        // the module (and its fixed array) load during device set-up, so the
+        // allocation-free entry point itself never causes a device
+        // allocation.
+        fail_cuda(k200::noalloc_scratch_address(&d.noalloc_scratch), "cudaGetSymbolAddress(noalloc scratch)");
         d.ready = true;
     }
     return d;
@@ -646,10 +652,11 @@ int gather_wait(int id, const unsigned *flags, int ranks, int rank) {
 
 // Rowwise-int8 matmul whose activation scratch is the module's static array
 // instead of the Kernel's grown buffer.  Same contract, kernels and results as
-// kunlun::matmul(..., rowwise_i8, ...).  Nothing here allocates: the size
-// check comes before any CUDA call, the device must already be set up (its
-// stream and error word are created by the first select), and the scratch
-// address is looked up once per device.
+// kunlun::matmul(..., rowwise_i8, ...), including the KUNLUN_TC switch.
+// Nothing here allocates: the size check comes before any CUDA call, and the
+// device must already be set up, since its first select creates its stream
+// and error word and loads the module that holds the scratch (whose address
+// it records).
 int matmul_i8_noalloc(int id, void *y, const void *w, const void *x, int k, int n, int batch, const float *scales,
                       const float *maximum) {
     using namespace kunlun;
@@ -674,18 +681,7 @@ int matmul_i8_noalloc(int id, void *y, const void *w, const void *x, int k, int 
         return kNoAllocNotReady;
     }
     kunlun::select(id);  // the state exists, so this only makes the device current
-    if (!d.noalloc_scratch) {
-        void *p = nullptr;
-        cudaError_t e = noalloc_scratch_address(&p);
-        if (e != cudaSuccess || !p) {
-            cudaGetLastError();
-            std::fprintf(stderr, "k200_matmul_i8_noalloc: cudaGetSymbolAddress failed on device %d: %s\n", id,
-                         cudaGetErrorString(e));
-            std::fflush(stderr);
-            return e != cudaSuccess ? (int)e : (int)cudaErrorInvalidSymbol;
-        }
-        d.noalloc_scratch = p;
-    }
+    if (!d.noalloc_scratch) return (int)cudaErrorInvalidSymbol;  // set-up records it or aborts
     const size_t count = (size_t)k * batch;
     int8_t *q = static_cast<int8_t *>(d.noalloc_scratch);
     float *maxima = reinterpret_cast<float *>(static_cast<char *>(d.noalloc_scratch) + kNoAllocParamsOffset);
@@ -710,6 +706,7 @@ int matmul_i8_noalloc(int id, void *y, const void *w, const void *x, int k, int 
     r.act_max = maxima;
     r.row_scale = scales;
     r.prefetch_weights = d.static_weights;
+    r.tensor_cores = d.tensor_cores;
     e = launch_gemv(r, d.info, d.stream);
     if (e != cudaSuccess) return (int)e;
     ++d.matmuls;

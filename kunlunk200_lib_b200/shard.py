@@ -80,6 +80,7 @@ class PeerExchange:
                 v.y[r] = bases[r] + b * self.n_pad * 4
                 v.flags[r] = bases[r] + flags_off
             v.counter = bases[rank] + flags_off + 64
+            v.rows = n
             self.views.append(v)
 
     @staticmethod

@@ -211,17 +211,43 @@ static void decode_row(const void *w, int type, int k, int row, float *out) {
 }
 
 void ko_matmul_gold(const void *w, int type, const float *x, int k, int n, int batch, double *y) {
-    /* bench/library-bench.cpp:121-123 (double accumulation, serial j) */
-    float *row = (float *)malloc((size_t)k * 4);
-    for (int r = 0; r < n; ++r) {
-        decode_row(w, type, k, r, row);
-        for (int b = 0; b < batch; ++b) {
-            double gold = 0;
-            for (int j = 0; j < k; ++j) gold += (double)row[j] * (double)x[(size_t)b * k + j];
-            y[(size_t)b * n + r] = gold;
+    /* bench/library-bench.cpp:121-123 (double accumulation, serial j).  Rows
+     * run in parallel and four columns share a pass over the row, each with
+     * its own serial sum, so every output is the same as the serial loop's. */
+#ifdef _OPENMP
+#pragma omp parallel
+#endif
+    {
+        float *row = (float *)malloc((size_t)k * 4);
+#ifdef _OPENMP
+#pragma omp for schedule(dynamic, 16)
+#endif
+        for (int r = 0; r < n; ++r) {
+            decode_row(w, type, k, r, row);
+            int b = 0;
+            for (; b + 4 <= batch; b += 4) {
+                const float *x0 = x + (size_t)b * k, *x1 = x0 + k, *x2 = x1 + k, *x3 = x2 + k;
+                double g0 = 0, g1 = 0, g2 = 0, g3 = 0;
+                for (int j = 0; j < k; ++j) {
+                    const double wj = (double)row[j];
+                    g0 += wj * (double)x0[j];
+                    g1 += wj * (double)x1[j];
+                    g2 += wj * (double)x2[j];
+                    g3 += wj * (double)x3[j];
+                }
+                y[(size_t)b * n + r] = g0;
+                y[(size_t)(b + 1) * n + r] = g1;
+                y[(size_t)(b + 2) * n + r] = g2;
+                y[(size_t)(b + 3) * n + r] = g3;
+            }
+            for (; b < batch; ++b) {
+                double gold = 0;
+                for (int j = 0; j < k; ++j) gold += (double)row[j] * (double)x[(size_t)b * k + j];
+                y[(size_t)b * n + r] = gold;
+            }
         }
+        free(row);
     }
-    free(row);
 }
 
 void ko_matvec_model(const void *w, int type, const float *x, int k, int n, int batch, float *y) {
@@ -367,13 +393,20 @@ int ko_a8_tensor(const float *x, size_t count, int8_t *q0, int8_t *q1, float *ma
 void ko_i8_matmul(const int8_t *wq, const float *scales, const int8_t *q0, const int8_t *q1,
                   float max0, float max1, int k, int n, int batch, float *y, int32_t *p0,
                   int32_t *p1) {
-    /* src/k200.cpp:231-232 + kernels/kunlun-combine.xpu:19 */
+    /* src/k200.cpp:231-232 + kernels/kunlun-combine.xpu:19.  The int32 dots
+     * are exact in any order; the combine runs per output as written there. */
     float scale0 = max0 / 127.0f, scale1 = max1 / 127.0f;
+#ifdef _OPENMP
+#pragma omp parallel for collapse(2) schedule(dynamic, 64)
+#endif
     for (int c = 0; c < batch; ++c)
         for (int r = 0; r < n; ++r) {
             int32_t d0 = 0, d1 = 0;
             const int8_t *wr = wq + (size_t)r * k;
             const int8_t *a0 = q0 + (size_t)c * k, *a1 = q1 + (size_t)c * k;
+#ifdef _OPENMP
+#pragma omp simd reduction(+ : d0, d1)
+#endif
             for (int j = 0; j < k; ++j) {
                 d0 += (int32_t)a0[j] * wr[j];
                 d1 += (int32_t)a1[j] * wr[j];

@@ -142,7 +142,7 @@ def test_reference_consumers_link_against_this_library():
 # a well-formed two-rank exchange view (dummy addresses) that each case then breaks
 _GATHER = ("v = K.GatherView()\nv.ranks, v.rank = 2, 0\n"
            "for r in range(2):\n    v.y[r] = 4096 * (r + 1)\n    v.flags[r] = 65536 * (r + 1)\n"
-           "v.counter = 1 << 20\n")
+           "v.counter = 1 << 20\nv.rows = 64\n")
 
 
 def _run_contract(snippet: str) -> subprocess.CompletedProcess:
@@ -174,6 +174,8 @@ def _run_contract(snippet: str) -> subprocess.CompletedProcess:
         ("gather wait on a bad exchange", _GATHER + "w = K.GatherView()\n"
                                           "K.matmul_q4_gather(0, v, 0, 16, 16, 4096, 16, 16, 64, wait_for=w)"),
         ("gather negative first row", _GATHER + "K.matmul_q4_gather(0, v, -16, 16, 16, 4096, 16, 16, 64)"),
+        ("gather rows past the buffer", _GATHER + "K.matmul_q4_gather(0, v, 56, 16, 16, 4096, 16, 16, 64)"),
+        ("gather without a row count", _GATHER + "v.rows = 0\nK.matmul_q4_gather(0, v, 0, 16, 16, 4096, 16, 16, 64)"),
         ("gather wait without ranks", _GATHER + "v.ranks = 0\nK.gather_wait(0, v)"),
     ],
 )

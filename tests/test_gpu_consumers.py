@@ -49,6 +49,24 @@ def test_library_bench_memory(K, gpu):
     assert "PASS" in out
 
 
+def test_peer_same_device(K, gpu):
+    """kunlun::peer (src/k200.cpp:89-95) with source and destination on one
+    device: the bytes arrive, the call completes before returning, and the
+    peer counters of Statistics move (src/k200.cpp:94, k200.h:345-350)."""
+    import numpy as np
+
+    nbytes = (1 << 20) + 48
+    data = (np.arange(nbytes, dtype=np.uint64) * 2654435761 % 251).astype(np.uint8)
+    src, dst = K.Buffer(0, nbytes), K.Buffer(0, nbytes)
+    src.upload(data)
+    before = K.statistics()
+    K.peer(0, dst.data(), 0, src.data(), nbytes)
+    assert np.array_equal(dst.download(np.uint8, nbytes), data)
+    after = K.statistics()
+    assert after["peer_copies"] == before["peer_copies"] + 1
+    assert after["peer_bytes"] == before["peer_bytes"] + nbytes
+
+
 def test_fused_bench(K, gpu):
     """bench/fused-bench.cpp: direct q4_0 within 1e-3(1+|ref|), fused vs two-FC i8 NMSE <= 1e-8."""
     out = _run("fused-bench", 0, 4096, 4096, 1)

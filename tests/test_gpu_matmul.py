@@ -28,6 +28,9 @@ TOL = 1e-5
 # NMSE < 1e-8 (measured ~4e-10 at K = 8192: the f32 accumulation inside the
 # tensor cores, not the ~2^-22 activation split, dominates).
 TOL_F16_TC = 1e-3
+# Batched Q4_0 on the tensor cores (W = d(q - 8) split into exact f16 hi + lo,
+# X into f16 hi + lo, three products, f32 accumulation).
+TOL_Q4_TC = 1e-3
 TC_MIN_BATCH = 4
 
 
@@ -123,7 +126,7 @@ def test_q4_0_batched_tensor_cores(K, O, gpu, k, n, batch):
     q4, x = _q4_case(O, k, n, batch)
     y = _device_matmul(K, K.Q4_0, q4, x, k, n, batch)
     gold = O.matmul_gold(q4, O.WT_Q4_0, x, k, n, batch)
-    _check_float(y, gold, tol=TOL_F16_TC)
+    _check_float(y, gold, tol=TOL_Q4_TC)
     assert np.sum((y - gold) ** 2) / np.sum(gold ** 2) < 1e-8
 
 
