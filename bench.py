@@ -203,6 +203,36 @@ def cpu_baseline(seconds: float = 10.0) -> dict:
                       f"FP64 reference() over pre-decoded weights, {dt:.1f} s"}
 
 
+def extra_cpu_baselines(seconds: float = 3.0) -> dict:
+    """The other two CPU paths of the reference on this path, timed on the host:
+    (a) library-bench's single-thread FP64 gold loop over the decoded Q4_0
+    weights (bench/library-bench.cpp:121-123), on the up projection; (c) the
+    per-call host quantiser of the rowwise-int8 path (src/k200.cpp:209-229,
+    two-pass per-tensor A8), on config 4's batch-32 activations."""
+    import oracle as O
+
+    k, n = UP
+    rows = 256
+    dec = O.q4_0_dequantize(O.q4_0_quantize(O.normal(11, rows * k, 0.0, 0.02), rows, k), rows, k)
+    x = O.uniform(0x09200ABC, k, -1.0, 1.0)
+    t0, done = time.perf_counter(), 0
+    while time.perf_counter() - t0 < seconds or done < 2:
+        O.reference_fp64(dec, x, k, rows, 1, threads=1)
+        done += 1
+    dt = time.perf_counter() - t0
+    gold = {"value": q4_bytes(k, rows) * done / dt / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"{done} calls of the serial FP64 gold loop over {rows} rows of K{k} ({dt:.1f} s)"}
+    xi = O.normal(0x09200ABC, 32 * 8192, 0.0, 1.0)
+    t0, done = time.perf_counter(), 0
+    while time.perf_counter() - t0 < seconds or done < 2:
+        O.a8_tensor(xi)
+        done += 1
+    dt = time.perf_counter() - t0
+    quant = {"value": dt / done * 1e3, "unit": "ms per call", "cores": 1, "kind": "port",
+             "sample": f"{done} two-pass per-tensor A8 quantisations of 32x8192 f32 activations ({dt:.1f} s)"}
+    return {"library_bench_gold_loop": gold, "i8_host_activation_quantiser": quant}
+
+
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -442,6 +472,9 @@ def run_ours(args) -> None:
     alg_up = q4_bytes(UP[0], n_up) + 4 * UP[0] + 4 * n_up
     alg_down = q4_bytes(DOWN[0], n_down) + 4 * DOWN[0] + 4 * n_down
     mean_up, mean_down = statistics.mean(d_up), statistics.mean(d_down)
+
+    def spread(d):
+        return {"median": statistics.median(d) * 1e3, "min": min(d) * 1e3, "max": max(d) * 1e3, "launches": len(d)}
     # the timed region runs nothing but the two GEMV launches per step (and,
     # on N > 1, one wait launch per graph), so its average GEMV duration is
     # the region's device time over its GEMV launches
@@ -454,30 +487,65 @@ def run_ours(args) -> None:
     xh = torch.empty(UP[0], dtype=torch.float32).pin_memory()
     xh.copy_(x.cpu())
     yh = torch.empty(DOWN[1], dtype=torch.float32).pin_memory()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t_wall = time.perf_counter()
+
+    def host_step(i: int):
+        """One decode step as a user issues it: input in, both GEMVs, output out."""
+        K.check(K.copy_async(x, xh, xh.numel() * 4, K.HOST_TO_DEVICE))
+        step(i)
+        finish(i)
+        K.check(K.copy_async(yh, output(i), yh.numel() * 4, K.DEVICE_TO_HOST))
+
+    def timed_e2e(run_step) -> tuple[float, float]:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        wall = time.perf_counter()
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for i in range(e2e_steps):
+                run_step(i)
+                K.check(K.wait())
+            e1.record(stream)
+        stream.synchronize()
+        wall = time.perf_counter() - wall
+        te = torch.tensor([e0.elapsed_time(e1)], device="cuda")
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        return total_bytes * e2e_steps / (float(te.item()) * 1e-3) / 1e9, wall
+
+    # (1) each step recorded once with k200_graph_* and replayed: one launch
+    #     per step (a graph per weight set; per output-buffer parity on N > 1)
+    ngraphs = sets if world == 1 else sets * 2 // math.gcd(sets, 2)
+    graphs = []
     with torch.cuda.stream(stream):
-        e0.record(stream)
-        for i in range(e2e_steps):
-            K.check(K.copy_async(x, xh, xh.numel() * 4, K.HOST_TO_DEVICE))
-            step(i)
-            finish(i)
-            K.check(K.copy_async(yh, output(i), yh.numel() * 4, K.DEVICE_TO_HOST))
+        for i in range(ngraphs):
+            host_step(i)  # a direct run first: nothing grows during the recording
             K.check(K.wait())
-        e1.record(stream)
-    stream.synchronize()
-    t_wall = time.perf_counter() - t_wall
-    e2e_ms = e0.elapsed_time(e1)
-    te = torch.tensor([e2e_ms], device="cuda")
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_ms = float(te.item())
-    e2e_value = total_bytes * e2e_steps / (e2e_ms * 1e-3) / 1e9
+            g = K.Graph(dev)
+            with g:
+                host_step(i)
+            graphs.append(g)
+    e2e_value, t_wall = timed_e2e(lambda i: graphs[i % ngraphs].launch())
+    # (2) the same calls issued one by one
+    e2e_eager, t_wall_eager = timed_e2e(host_step)
+    for g in graphs:
+        g.close()
 
     cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
+    if cpu is not None:
+        cpu["also"] = extra_cpu_baselines()
+
+    # the batched half of the metric (configs 2-4), same process, same GPUs
+    batched = None
+    if not args.no_batched:
+        batched = []
+        for wname, bk, bn, bb, blabel in BATCHED_SET:
+            r = measure_gemm(K, torch, dist, dev, stream, world, rank, wname, bk, bn, bb, 0, 3, blabel,
+                             target_s=0.4)
+            if r is not None:
+                batched.append({key: r[key] for key in ("metric", "value", "unit", "ms_per_step", "steps", "dtype",
+                                                        "config", "roofline", "e2e", "gpu_launches", "clocks")})
 
     # the committed capture is of full-size launches; a shard's launch streams
     # its rows' share of the weights (traffic tracks the algorithmic bytes)
@@ -505,21 +573,27 @@ def run_ours(args) -> None:
                          "traffic": shard_traffic,
                          "kernel": "q4_mma_gemv_kernel",
                          "launch_us": launch_ms * 1e3,
-                         "isolated_launch_us": {"up": mean_up * 1e3, "down": mean_down * 1e3},
+                         "isolated_launch_us": {"up": mean_up * 1e3, "down": mean_down * 1e3,
+                                                "up_spread": spread(d_up), "down_spread": spread(d_down)},
                          "algorithmic_bytes_per_launch": {"up": alg_up, "down": alg_down}},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": xh.numel() * 4,
                     "d2h_bytes_per_step": yh.numel() * 4, "steps": e2e_steps,
-                    "path": ("k200_copy_async H2D + 2x k200_matmul + k200_copy_async D2H + k200_wait per step"
+                    "path": ("k200_graph_launch of the recorded step (k200_copy_async H2D, 2x k200_matmul, "
+                             "k200_copy_async D2H) + k200_wait per step"
                              if world == 1 else
-                             "k200_copy_async H2D + 2x k200_matmul_q4_gather + k200_gather_wait + "
-                             "k200_copy_async D2H + k200_wait per step"),
-                    "wall_s": t_wall},
+                             "k200_graph_launch of the recorded step (k200_copy_async H2D, 2x "
+                             "k200_matmul_q4_gather, k200_gather_wait, k200_copy_async D2H) + k200_wait per step"),
+                    "wall_s": t_wall,
+                    "eager": {"value": e2e_eager, "wall_s": t_wall_eager,
+                              "path": "the same calls issued one by one through the C ABI, k200_wait per step"}},
             "gpu_launches": launches,
             "clocks": clock_info,
         }
         if world > 1:
             line["config"]["nvlink_bytes_per_step"] = 4 * (UP[1] + DOWN[1]) * (world - 1)
+        if batched is not None:
+            line["batched"] = batched
         print(json.dumps(line), flush=True)
     K.set_stream(dev, None)
     del g_main, g_rem
@@ -600,32 +674,24 @@ def gemm_cpu_rate(wname: str, k: int, n: int, batch: int, seconds: float, sample
     return 2.0 * rows * k * batch * done / dt / 1e12, cores, kind, sample
 
 
-def run_gemm(args) -> None:
-    import torch
-    import torch.distributed as dist
+def gemm_dtype(wname: str) -> str:
+    return {"q4_0": "f16 hi/lo x f16 hi/lo", "f16": "f16 x f16 hi/lo", "f32": "f32", "rowwise_i8": "int8"}[wname]
 
-    import kunlunk200_lib_b200 as K
+
+def measure_gemm(K, torch, dist, dev: int, stream, world: int, rank: int, wname: str, k: int, n: int,
+                 batch: int, steps: int, warmup: int, label: str, cpu_seconds: float = 0.0,
+                 target_s: float = 0.0) -> dict | None:
+    """One batched matmul configuration: rotating
+    resident weights (> 2x L2), CUDA-graph steps timed with CUDA events on the
+    launching stream (max over ranks), clocks sampled during the timed
+    region, and the same steps end to end through the C ABI.  With
+    target_s > 0 the step count is chosen so the timed region lasts about
+    that long.  Returns rank 0's JSON line (None on other ranks)."""
     from kunlunk200_lib_b200.shard import row_shard
 
-    wname, k, n, batch, label = gemm_shape(args)
     wtype = {"q4_0": K.Q4_0, "f16": K.F16, "f32": K.F32, "rowwise_i8": K.ROWWISE_I8}[wname]
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world != args.gpus:
-        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
     if n % world:
         raise SystemExit(f"N={n} does not split evenly over {world} GPUs")
-    torch.cuda.set_device(local)
-    if world > 1:
-        import datetime
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
-    dev = local
-    K.select(dev)
-    stream = torch.cuda.Stream()
-    K.set_stream(dev, stream.cuda_stream)
-    K.set_static_weights(dev, True)
     l2 = torch.cuda.get_device_properties(dev).L2_cache_size
     n_sh = row_shard(n, world, rank)[1]
     shard_bytes = gemm_weight_bytes(K, wname, k, n_sh)
@@ -670,13 +736,24 @@ def run_gemm(args) -> None:
         if world > 1:
             dist.all_gather_into_tensor(y_full, y_sh)
 
+    nwarm = max(3, warmup)
+    w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
-        for i in range(max(3, args.warmup)):
+        step(0)  # first call: scratch growth, kernel set-up
+        w0.record(stream)
+        for i in range(1, nwarm):
             step(i)
+        w1.record(stream)
     stream.synchronize()
     K.check(K.wait())
+    if target_s > 0:
+        est = w0.elapsed_time(w1) / max(1, nwarm - 1) * 1e-3
+        t = torch.tensor([est], device="cuda")
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        steps = int(min(4000, max(20, target_s / max(float(t.item()), 1e-6))))
     per_graph = sets * max(1, 24 // sets)
-    reps, rem = divmod(args.steps, per_graph)
+    reps, rem = divmod(steps, per_graph)
 
     def capture(nsteps: int):
         if nsteps == 0:
@@ -727,20 +804,23 @@ def run_gemm(args) -> None:
         dist.barrier()
         torch.cuda.synchronize()
     flops_step = 2.0 * n * k * batch
-    value = flops_step * args.steps / (ms * 1e-3) / 1e12
-    ms_step = ms / args.steps
+    value = flops_step * steps / (ms * 1e-3) / 1e12
+    ms_step = ms / steps
     # kernels of ours per matmul: the activation preparation (f16/q4_0 hi/lo
     # split; rowwise-int8 quantiser: one CTA up to 64K elements, else three
     # passes) and the matmul kernel itself
     tc = batch >= 4 and k % 16 == 0 and (wname != "q4_0" or k % 256 == 0) and wname != "f32"
     prep = (1 if (tc and wname in ("q4_0", "f16")) else 0) + ((1 if batch * k <= 65536 else 3) if i8 else 0)
-    launches = args.steps * (1 + prep)
+    launches = steps * (1 + prep)
     peaks = read_peaks()
     hbm_gbs = shard_bytes / (ms_step * 1e-3) / 1e9
     tflops_gpu = flops_step / world / (ms_step * 1e-3) / 1e12
     tensor_peak = peaks["bf16_tflops"] * (2 if i8 else 1)
     hbm_frac, tensor_frac = hbm_gbs / peaks["hbm_gbs"], tflops_gpu / tensor_peak
     bound = "tensor" if tensor_frac > hbm_frac else "hbm"
+    f32_gemm = wname == "f32" and batch >= 9 and k % 64 == 0
+    kernel = ({"q4_0": "gemm_q4_kernel", "f16": "gemm_f16_kernel", "rowwise_i8": "gemm_i8_kernel"}[wname] if tc
+              else "gemm_f32_kernel" if f32_gemm else "gemv_stream_kernel")
     roof = {"bound": bound,
             "achieved": tflops_gpu if bound == "tensor" else hbm_gbs,
             "peak": tensor_peak if bound == "tensor" else peaks["hbm_gbs"],
@@ -749,12 +829,9 @@ def run_gemm(args) -> None:
             "hbm": {"achieved": hbm_gbs, "frac": hbm_frac},
             "tensor": {"achieved": tflops_gpu, "frac": tensor_frac,
                        "peak_note": ("2x measured bf16 (dense int8 rate)" if i8 else "measured bf16")},
-            "peak_source": peaks["source"], "traffic": None,
-            "kernel": {"q4_0": "gemm_q4_kernel", "f16": "gemm_f16_kernel", "f32": "gemv_stream_kernel",
-                       "rowwise_i8": "gemm_i8_kernel"}[wname] if tc or wname == "f32" else "gemv_stream_kernel",
-            "launch_us": ms_step * 1e3}
+            "peak_source": peaks["source"], "traffic": None, "kernel": kernel, "launch_us": ms_step * 1e3}
     # end to end through the C ABI: pinned host X in, pinned host Y out, every step
-    e2e_steps = min(args.steps, 500)
+    e2e_steps = max(10, min(steps, 500))
     xh = torch.empty((batch, k), dtype=torch.float32).pin_memory()
     xh.copy_(x.cpu())
     yh = torch.empty(y_full.numel(), dtype=torch.float32).pin_memory()
@@ -776,31 +853,67 @@ def run_gemm(args) -> None:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_value = flops_step * e2e_steps / (float(te.item()) * 1e-3) / 1e12
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, cores, kind, sample = gemm_cpu_rate(wname, k, n, batch, 10.0)
+    if rank == 0 and world == 1 and cpu_seconds > 0:
+        v, cores, kind, sample = gemm_cpu_rate(wname, k, n, batch, cpu_seconds)
         cpu = {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": kind, "sample": sample}
-    if rank == 0:
-        unit = "TOP/s" if i8 else "TFLOP/s"
-        line = {
-            "metric": f"{wname}_batched_matmul_tflops", "value": value, "unit": unit, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": {"q4_0": "f16 hi/lo x f16 hi/lo", "f16": "f16 x f16 hi/lo",
-                                                                "f32": "f32", "rowwise_i8": "int8"}[wname],
-            "data": "synthetic",
-            "config": {"workload": f"{wname} matmul K{k} N{n} batch {batch} ({label})", "k": k, "n": n, "batch": batch,
-                       "parallelism": f"row-shard{world}+allgather" if world > 1 else "single",
-                       "work": "logical 2*N*K*batch per step",
-                       "l2": f"{sets} rotating weight sets ({sets * shard_bytes / 1e6:.0f} MB per GPU)",
-                       "timing": "CUDA graph replays, CUDA events on the launching stream, max over ranks"},
-            "roofline": roof, "cpu_baseline": cpu,
-            "e2e": {"value": e2e_value, "unit": unit, "h2d_bytes_per_step": xh.numel() * 4,
-                    "d2h_bytes_per_step": yh.numel() * 4, "steps": e2e_steps,
-                    "path": "k200_copy_async H2D + k200_matmul + k200_copy_async D2H + k200_wait per step"},
-            "gpu_launches": launches, "clocks": clock_info,
-        }
+    del g_main, g_rem
+    kern.close()
+    del weights
+    torch.cuda.synchronize()
+    if rank != 0:
+        return None
+    unit = "TOP/s" if i8 else "TFLOP/s"
+    return {
+        "metric": f"{wname}_batched_matmul_tflops", "value": value, "unit": unit, "n_gpus": world,
+        "steps": steps, "warmup": warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": gemm_dtype(wname), "data": "synthetic",
+        "config": {"workload": f"{wname} matmul K{k} N{n} batch {batch} ({label})", "k": k, "n": n, "batch": batch,
+                   "parallelism": f"row-shard{world}+allgather" if world > 1 else "single",
+                   "work": "logical 2*N*K*batch per step",
+                   "l2": f"{sets} rotating weight sets ({sets * shard_bytes / 1e6:.0f} MB per GPU)",
+                   "timing": "CUDA graph replays, CUDA events on the launching stream, max over ranks"},
+        "roofline": roof, "cpu_baseline": cpu,
+        "e2e": {"value": e2e_value, "unit": unit, "h2d_bytes_per_step": xh.numel() * 4,
+                "d2h_bytes_per_step": yh.numel() * 4, "steps": e2e_steps,
+                "path": "k200_copy_async H2D + k200_matmul + k200_copy_async D2H + k200_wait per step"},
+        "gpu_launches": launches, "clocks": clock_info,
+    }
+
+
+# The batched half of the metric, measured in the default run beside the
+# batch-1 GEMV (BASELINE configs 2-4 at their prefill / decode-batch sizes).
+BATCHED_SET = [("q4_0", 4096, 14336, 128, "config 2"), ("q4_0", 4096, 14336, 512, "config 2"),
+               ("f16", 8192, 8192, 64, "config 3"), ("f32", 8192, 8192, 64, "config 3"),
+               ("rowwise_i8", 8192, 28672, 256, "config 4")]
+
+
+def run_gemm(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    import kunlunk200_lib_b200 as K
+
+    wname, k, n, batch, label = gemm_shape(args)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dev = local
+    K.select(dev)
+    stream = torch.cuda.Stream()
+    K.set_stream(dev, stream.cuda_stream)
+    K.set_static_weights(dev, True)
+    line = measure_gemm(K, torch, dist, dev, stream, world, rank, wname, k, n, batch, args.steps, args.warmup, label,
+                        cpu_seconds=0.0 if args.no_cpu_baseline else 10.0)
+    if line is not None:
         print(json.dumps(line), flush=True)
     K.set_stream(dev, None)
-    del g_main, g_rem
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -831,6 +944,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=200)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-batched", action="store_true", help="default workload: skip the batched configs 2-4")
     ap.add_argument("--workload", choices=["gemv"] + sorted(GEMM_CONFIGS), default="gemv",
                     help="gemv: config 1 (the metric's workload, default); others: BASELINE configs 2-4")
     ap.add_argument("--batch", type=int, default=0, help="batched workloads: activation columns")

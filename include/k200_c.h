@@ -85,6 +85,24 @@ void k200_set_static_weights(int device, int enabled);
 /* Asynchronous copy on the library stream of the current device (pinned host
  * memory makes it truly asynchronous); completion via k200_wait(). */
 int k200_copy_async(void *dst, const void *src, size_t bytes, int kind);
+/* CUDA graphs of library work.  k200_graph_begin starts capturing the
+ * library stream of `device`; the calls that follow on this thread that only
+ * submit work (k200_copy_async, k200_matmul, k200_matmul_q4_gather, ...) are
+ * recorded instead of run, and k200_graph_end turns the record into a
+ * replayable graph (*graph, a cudaGraphExec_t).  k200_graph_launch replays it
+ * on the library stream (completion via k200_select + k200_wait), with the
+ * pointers, shapes and host buffers it was recorded with: a decode step of
+ * H2D input, the chained matmuls and D2H output becomes one launch, and the
+ * kernels keep their programmatic-launch overlap.  Calls that complete
+ * before returning (k200_wait, k200_copy, elementwise, ...) or that grow
+ * scratch (the first matmul of a Kernel at a new size) fail during a
+ * capture, so run the sequence once before recording it.  Other threads must
+ * not submit work to the device while it is being recorded (hold k200_lock).
+ * Replays do not move the matmul counters.  0 or a CUDA error code. */
+int k200_graph_begin(int device);
+int k200_graph_end(int device, void **graph);
+int k200_graph_launch(int device, void *graph);
+int k200_graph_destroy(void *graph);
 /* GGML Q4_0 quantiser on the device: f32 [n][k] (device) -> 18-byte blocks
  * [n][k/32] (device).  Asynchronous on the library stream. */
 void k200_quantize_q4_0(int device, void *q4, const float *w, int k, int n);
@@ -269,6 +287,17 @@ int k200_matmul_q4_gather(int device, const k200_gather *out, int row_begin, con
                           int n, void *scratch, size_t scratch_bytes, const k200_gather *wait_for);
 /* The wait alone (for the last exchange of a sequence). */
 int k200_gather_wait(int device, const k200_gather *exchange);
+/* Row gather for any row-sharded matmul (any weight type and batch, any
+ * split of the rows, uneven ones included): this rank's slice, [batch][n]
+ * floats at `shard` (device memory, e.g. the y of a k200_matmul over this
+ * rank's n weight rows), is stored into columns [row_begin, row_begin + n) of
+ * every rank's [batch][rows] output buffer, then the exchange's epoch is
+ * published as k200_matmul_q4_gather does; readers wait with
+ * k200_gather_wait (or wait_for).  Each buffer y[r] must hold batch * rows
+ * floats.  Asynchronous on the library stream; 0 or a CUDA error code.
+ * Replaces the reference consumers' per-slice kunlun::peer copies of a row
+ * split (src/k200.cpp:89-95, docs/common-q4.md "Row Split"). */
+int k200_gather_rows(int device, const k200_gather *out, int row_begin, const float *shard, int n, int batch);
 
 #ifdef __cplusplus
 }

@@ -61,6 +61,10 @@ _SIGNATURES = {
     "k200_stream": (C.c_void_p, [C.c_int]),
     "k200_set_stream": (None, [C.c_int, C.c_void_p]),
     "k200_set_static_weights": (None, [C.c_int, C.c_int]),
+    "k200_graph_begin": (C.c_int, [C.c_int]),
+    "k200_graph_end": (C.c_int, [C.c_int, C.POINTER(C.c_void_p)]),
+    "k200_graph_launch": (C.c_int, [C.c_int, C.c_void_p]),
+    "k200_graph_destroy": (C.c_int, [C.c_void_p]),
     "k200_quantize_q4_0": (None, [C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int]),
     "k200_ipc_handle": (C.c_int, [C.c_void_p, C.c_void_p]),
     "k200_ipc_open": (C.c_int, [C.c_int, C.c_void_p, C.POINTER(C.c_void_p)]),
@@ -69,6 +73,7 @@ _SIGNATURES = {
     "k200_matmul_q4_gather": (C.c_int, [C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
                                         C.c_void_p, C.c_size_t, C.c_void_p]),
     "k200_gather_wait": (C.c_int, [C.c_int, C.c_void_p]),
+    "k200_gather_rows": (C.c_int, [C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int]),
     "k200_matmul_i8_noalloc": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
                                          C.c_void_p, C.c_void_p]),
     # native Q4 layout
@@ -238,6 +243,45 @@ def set_stream(device: int, stream_handle: int | None) -> None:
 def set_static_weights(device: int, enabled: bool) -> None:
     """Weights of `device`'s matmuls are never written by the kernel just before them."""
     lib().k200_set_static_weights(device, 1 if enabled else 0)
+
+
+class Graph:
+    """A recorded sequence of library work on one device (k200_graph_*).
+
+    with K.Graph(dev) as g:        # records instead of running
+        K.copy_async(...); K.matmul(...); ...
+    g.launch(); K.select(dev); K.check(K.wait())
+    """
+
+    def __init__(self, device: int):
+        self.device = device
+        self.handle = None
+
+    def __enter__(self):
+        check(lib().k200_graph_begin(self.device))
+        return self
+
+    def __exit__(self, exc_type, exc, tb):
+        out = C.c_void_p()
+        rc = lib().k200_graph_end(self.device, C.byref(out))
+        if exc_type is None:
+            check(rc)
+            self.handle = out.value
+        return False
+
+    def launch(self) -> None:
+        check(lib().k200_graph_launch(self.device, self.handle))
+
+    def close(self) -> None:
+        if self.handle:
+            check(lib().k200_graph_destroy(self.handle))
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class runtime_lock:
@@ -759,6 +803,12 @@ def matmul_q4_gather(device: int, out: GatherView, row_begin: int, w, x, k: int,
     """
     return lib().k200_matmul_q4_gather(device, C.addressof(out), row_begin, _ptr(w), _ptr(x), k, n, _ptr(scratch),
                                        scratch_bytes, None if wait_for is None else C.addressof(wait_for))
+
+
+def gather_rows(device: int, out: GatherView, row_begin: int, shard, n: int, batch: int = 1) -> int:
+    """This rank's [batch][n] slice into columns row_begin.. of every rank's [batch][rows] output
+    (k200_gather_rows); 0 or a CUDA error code, asynchronous on the library stream."""
+    return lib().k200_gather_rows(device, C.addressof(out), row_begin, _ptr(shard), n, batch)
 
 
 def gather_wait(device: int, exchange: GatherView) -> int:

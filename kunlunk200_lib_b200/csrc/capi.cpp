@@ -20,6 +20,7 @@ size_t peer_byte_count();
 int matmul_q4_gather(int device, const GatherLaunch &g, const void *w, const void *x, int k, int n, void *scratch,
                      size_t scratch_bytes);
 int gather_wait(int device, const unsigned *flags, int ranks, int rank);
+int gather_rows(int device, const GatherLaunch &g, const float *shard, int n, int batch, int rows);
 size_t q4_gather_scratch(int device, int k, int n);
 }  // namespace k200
 
@@ -93,6 +94,50 @@ void *k200_stream(int device) { return static_cast<void *>(k200::library_stream(
 void k200_set_stream(int device, void *stream) { k200::set_stream(device, static_cast<cudaStream_t>(stream)); }
 
 void k200_set_static_weights(int device, int enabled) { k200::set_static_weights(device, enabled != 0); }
+
+// ---- CUDA graphs of library work ----------------------------------------------
+int k200_graph_begin(int device) {
+    std::lock_guard<std::recursive_mutex> lock(kunlun::runtime_mutex());
+    kunlun::select(device);
+    const cudaError_t e = cudaStreamBeginCapture(k200::library_stream(device), cudaStreamCaptureModeThreadLocal);
+    if (e != cudaSuccess) cudaGetLastError();
+    return (int)e;
+}
+
+int k200_graph_end(int device, void **graph) {
+    std::lock_guard<std::recursive_mutex> lock(kunlun::runtime_mutex());
+    kunlun::require(graph != nullptr);
+    kunlun::select(device);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(k200::library_stream(device), &g);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        if (g) cudaGraphDestroy(g);
+        return (int)e;
+    }
+    cudaGraphExec_t exec = nullptr;
+    e = cudaGraphInstantiate(&exec, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return (int)e;
+    }
+    *graph = static_cast<void *>(exec);
+    return 0;
+}
+
+int k200_graph_launch(int device, void *graph) {
+    std::lock_guard<std::recursive_mutex> lock(kunlun::runtime_mutex());
+    kunlun::require(graph != nullptr);
+    kunlun::select(device);
+    return (int)cudaGraphLaunch(static_cast<cudaGraphExec_t>(graph), k200::library_stream(device));
+}
+
+int k200_graph_destroy(void *graph) {
+    std::lock_guard<std::recursive_mutex> lock(kunlun::runtime_mutex());
+    if (!graph) return 0;
+    return (int)cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(graph));
+}
 
 int k200_copy_async(void *dst, const void *src, size_t bytes, int kind) {
     std::lock_guard<std::recursive_mutex> lock(kunlun::runtime_mutex());
@@ -190,6 +235,20 @@ int k200_matmul_q4_gather(int device, const k200_gather *out, int row_begin, con
         g.wait_rank = wait_for->rank;
     }
     return k200::matmul_q4_gather(device, g, w, x, k, n, scratch, scratch_bytes);
+}
+
+int k200_gather_rows(int device, const k200_gather *out, int row_begin, const float *shard, int n, int batch) {
+    kunlun::require(gather_ok(out) && shard && row_begin >= 0 && n > 0 && batch > 0);
+    kunlun::require(n <= out->rows && row_begin <= out->rows - n);
+    k200::GatherLaunch g;
+    g.ranks = out->ranks;
+    g.rank = out->rank;
+    for (int r = 0; r < out->ranks; ++r) {
+        g.y[r] = out->y[r] + row_begin;
+        g.flags[r] = out->flags[r];
+    }
+    g.counter = out->counter;
+    return k200::gather_rows(device, g, shard, n, batch, out->rows);
 }
 
 int k200_gather_wait(int device, const k200_gather *exchange) {

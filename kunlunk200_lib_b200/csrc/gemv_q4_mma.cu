@@ -60,6 +60,7 @@
 
 #include "device_common.cuh"
 #include "k200_internal.h"
+#include "peer_flags.cuh"
 
 namespace k200 {
 
@@ -307,37 +308,6 @@ __device__ __forceinline__ void st_relaxed(unsigned long long *p, unsigned long 
 }
 constexpr unsigned long long kPresent = 1ull << 32;
 constexpr uint32_t kPeerBudget = 1u << 20;   // polls of a partial sum (with 64 ns sleeps)
-
-// Flags of the fused all-gather live in every rank's memory and are written
-// by other GPUs: system-scope acquire loads and release stores.
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-// Polls of another rank's flag, with short sleeps (a flag that arrives is
-// seen within a fraction of a microsecond): several seconds in all, because
-// ranks are separate processes whose hosts can fall behind one another (a
-// pause in one process) while the other rank's GPU already waits.
-constexpr uint32_t kFlagBudget = 1u << 23;
-// Waits until every rank's entry of this rank's flag array has reached this
-// rank's own entry (epochs only grow; compared modulo 2^32).  Single thread.
-__device__ __forceinline__ void wait_peer_flags(const unsigned *flags, int ranks, int rank, int *err) {
-    const unsigned target = ld_acquire_sys(flags + rank);
-    for (int r = 0; r < ranks; ++r) {
-        if (r == rank) continue;
-        for (uint32_t spin = 0; static_cast<int>(ld_acquire_sys(flags + r) - target) < 0; ++spin) {
-            if (spin >= kFlagBudget) {
-                atomicExch(err, kErrPeerTimeout);
-                break;
-            }
-            __nanosleep(200);
-        }
-    }
-}
 
 // kGather: the fused all-gather (xg.ranks > 0) and the wait for X
 // (xg.wait_flags), in a separate instantiation with its own parameter, so that
@@ -593,17 +563,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // fence, which orders them before its arrival (one fence per block;
         // a fence in every thread costs microseconds each).
         consumer_sync();
-        if (tid == 0) {
-            __threadfence_system();
-            const unsigned arrived = atomicAdd(xg.counter, 1u) + 1u;
-            if (arrived == static_cast<unsigned>(a.grid)) {
-                __threadfence_system();
-                xg.counter[0] = 0u;  // the next launch's blocks arrive after this one completes
-                const unsigned epoch = xg.counter[1] + 1u;
-                xg.counter[1] = epoch;
-                for (int r = 0; r < xg.ranks; ++r) st_release_sys(xg.flags[r] + xg.rank, epoch);
-            }
-        }
+        if (tid == 0) publish_epoch(xg, a.grid);
     }
 }
 

@@ -77,6 +77,11 @@ cudaError_t launch_q4_mma_gemv(const GemvRequest &r, const DeviceInfo &dev, cuda
 // exchange has reached this rank's own (kErrPeerTimeout after its budget).
 cudaError_t launch_gather_wait(const unsigned *flags, int ranks, int rank, const DeviceInfo &dev,
                                cudaStream_t stream);
+// Row gather (gather.cu): [batch][n] slice -> columns of every rank's
+// [batch][rows] output (xg.y[r] point at the slice's first column), then the
+// exchange's next epoch.
+cudaError_t launch_gather_rows(const GatherLaunch &xg, const float *shard, int n, int batch, int rows,
+                               const DeviceInfo &dev, cudaStream_t stream);
 // Row gathers (get_rows.cu); an index outside [0, n) writes no output and
 // sets *status to 1 (else 0).
 cudaError_t launch_get_rows_f32(float *out, const float *in, const int32_t *idx, int *status, int k, int n, int rows,

@@ -640,6 +640,17 @@ int matmul_q4_gather(int id, const GatherLaunch &g, const void *w, const void *x
     return 0;
 }
 
+int gather_rows(int id, const GatherLaunch &g, const float *shard, int n, int batch, int rows) {
+    using namespace kunlun;
+    std::lock_guard<std::recursive_mutex> lock(mutex);
+    require(id >= 0 && id < cuda_device_count() && shard && n > 0 && batch > 0 && rows >= n);
+    require(g.ranks >= 1 && g.ranks <= kGatherMaxRanks && g.rank >= 0 && g.rank < g.ranks && g.counter);
+    require((size_t)batch * (size_t)rows <= (size_t)INT_MAX);
+    select(id);
+    DeviceState &d = state(id);
+    return (int)launch_gather_rows(g, shard, n, batch, rows, d.info, d.stream);
+}
+
 int gather_wait(int id, const unsigned *flags, int ranks, int rank) {
     using namespace kunlun;
     std::lock_guard<std::recursive_mutex> lock(mutex);

@@ -1,15 +1,18 @@
 """Row sharding of a matmul over the GPUs of one node.
 
 Each rank owns a contiguous slice of the output rows N of every weight
-(W[n_begin:n_begin+n_count, :]) and computes Y[:, slice]; an all-gather of
-the slices (NCCL over NVLink) rebuilds the full Y on every rank.  The
-reference library has no multi-device matmul of its own: its consumers
-split rows across devices and exchange them with kunlun::peer copies
-(src/k200.cpp:89-95); here the exchange is one collective.
+(W[n_begin:n_begin+n_count, :]) and computes Y[:, slice]; the slices are
+then gathered so every rank holds the full Y.  The reference library has no
+multi-device matmul of its own: its consumers split rows across devices and
+exchange them with kunlun::peer copies (src/k200.cpp:89-95).  Here the
+exchange runs over NVLink peer memory inside the library (PeerExchange with
+k200_matmul_q4_gather or k200_gather_rows: every slice is stored at its own
+offset, so uneven splits need no padding); row_shard also serves callers
+that gather with an NCCL all-gather, which needs equal sizes: padded_rows
+and gather_rows pad every slice to the largest one and drop the padding.
 
 Slices are as even as possible (the first N % world ranks own one extra
-row).  all_gather_into_tensor needs equal sizes, so every rank contributes
-a slice padded to the largest one and the padding is dropped afterwards.
+row).
 """
 from __future__ import annotations
 
@@ -51,12 +54,14 @@ def gather_rows(gathered, n: int, world: int, batch: int = 1):
 
 
 class PeerExchange:
-    """One all-gather exchange of a row-sharded batch-1 Q4_0 GEMV (k200_matmul_q4_gather).
+    """One all-gather exchange of a row-sharded matmul over peer memory
+    (k200_matmul_q4_gather for the batch-1 Q4_0 GEMV, k200_gather_rows for any
+    matmul).
 
     Every rank owns one device region, zeroed at creation:
-      ``buffers`` output buffers of the full ``n`` rows (floats, each padded to
-      a multiple of 64), then the exchange's flag array (``world`` words,
-      padded to 64 bytes), then this rank's two counter words.
+      ``buffers`` output buffers of [batch][n] floats (each padded to a
+      multiple of 64 floats), then the exchange's flag array (``world``
+      words, padded to 64 bytes), then this rank's two counter words.
     ``bases[r]`` is rank r's region as an address valid on this rank's device
     (its own allocation, or an IPC mapping of the other rank's).  ``view(b)``
     is the k200_gather of output buffer b; alternate buffers between
@@ -65,11 +70,12 @@ class PeerExchange:
     """
 
     def __init__(self, K, device: int, n: int, world: int, rank: int, bases: list[int], buffers: int = 2,
-                 owned=None, mapped=()):
-        if not 1 <= world <= K.GATHER_MAX_RANKS or not 0 <= rank < world or len(bases) != world:
-            raise ValueError(f"bad exchange: world={world} rank={rank} bases={len(bases)}")
+                 owned=None, mapped=(), batch: int = 1):
+        if not 1 <= world <= K.GATHER_MAX_RANKS or not 0 <= rank < world or len(bases) != world or batch < 1:
+            raise ValueError(f"bad exchange: world={world} rank={rank} bases={len(bases)} batch={batch}")
         self.K, self.device, self.n, self.world, self.rank, self.buffers = K, device, n, world, rank, buffers
-        self.n_pad = self.padded(n)
+        self.batch = batch
+        self.n_pad = self.padded(n * batch)
         self._owned, self._mapped = owned, list(mapped)
         flags_off = buffers * self.n_pad * 4
         self.views = []
@@ -88,22 +94,23 @@ class PeerExchange:
         return -(-n // 64) * 64
 
     @classmethod
-    def region_bytes(cls, n: int, buffers: int = 2) -> int:
-        return buffers * cls.padded(n) * 4 + 128
+    def region_bytes(cls, n: int, buffers: int = 2, batch: int = 1) -> int:
+        return buffers * cls.padded(n * batch) * 4 + 128
 
     @classmethod
-    def _region(cls, K, device: int, n: int, buffers: int):
+    def _region(cls, K, device: int, n: int, buffers: int, batch: int = 1):
         import numpy as np
 
-        nbytes = cls.region_bytes(n, buffers)
+        nbytes = cls.region_bytes(n, buffers, batch)
         buf = K.Buffer(device, nbytes)
         buf.upload(np.zeros(nbytes, np.uint8))
         return buf
 
     @classmethod
-    def over_group(cls, K, device: int, n: int, world: int, rank: int, all_gather, buffers: int = 2):
+    def over_group(cls, K, device: int, n: int, world: int, rank: int, all_gather, buffers: int = 2,
+                   batch: int = 1):
         """Collective: one region per rank, IPC handles swapped with ``all_gather(obj) -> list``."""
-        buf = cls._region(K, device, n, buffers)
+        buf = cls._region(K, device, n, buffers, batch)
         handles = all_gather(K.ipc_handle(buf.data()))
         bases, mapped = [], []
         for r, h in enumerate(handles):
@@ -113,14 +120,14 @@ class PeerExchange:
                 p = K.ipc_open(device, h)
                 bases.append(p)
                 mapped.append(p)
-        return cls(K, device, n, world, rank, bases, buffers, owned=buf, mapped=mapped)
+        return cls(K, device, n, world, rank, bases, buffers, owned=buf, mapped=mapped, batch=batch)
 
     @classmethod
-    def on_one_device(cls, K, device: int, n: int, world: int, buffers: int = 2):
+    def on_one_device(cls, K, device: int, n: int, world: int, buffers: int = 2, batch: int = 1):
         """All ranks' regions on one device, for running the ranks one after another in one stream."""
-        bufs = [cls._region(K, device, n, buffers) for _ in range(world)]
+        bufs = [cls._region(K, device, n, buffers, batch) for _ in range(world)]
         bases = [b.data() for b in bufs]
-        xs = [cls(K, device, n, world, r, bases, buffers) for r in range(world)]
+        xs = [cls(K, device, n, world, r, bases, buffers, batch=batch) for r in range(world)]
         xs[0]._owned = bufs  # the first rank's object keeps every region alive
         return xs
 
@@ -128,7 +135,7 @@ class PeerExchange:
         return self.views[b % self.buffers]
 
     def output(self, b: int) -> int:
-        """Address of this rank's own output buffer b (the full n rows)."""
+        """Address of this rank's own output buffer b (the full [batch][n] rows)."""
         return self.views[b % self.buffers].y[self.rank]
 
     def close(self) -> None:

@@ -78,6 +78,14 @@ def test_memory_example(K, gpu):
     assert "PASS" in out
 
 
+def test_cmake_package_consumer(K, gpu):
+    """The reference's examples/library project, configured unchanged with
+    find_package(KunlunK200) against this repository's CMake install
+    (`make -C oracle cmake-consumer`), runs against that installed library."""
+    out = _run("cmake-consumer")
+    assert "KunlunK200 0.7.12: PASS" in out, out
+
+
 # bench/native-q4-bench.cpp: mode PD K N batch dtype pattern trials.  The
 # program requires NMSE < 1e-5 (W4A8x2 path), < 1e-10 (exact fallback) or
 # < 1e-2 (cdnn) against its FP64 reference, and re-checks the native pack

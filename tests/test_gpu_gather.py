@@ -153,3 +153,53 @@ def test_gather_two_gpus(K, gpu):
     p = subprocess.run(["timeout", "-k", "30", "240"] + cmd, cwd=ROOT, env=env, capture_output=True, text=True)
     assert p.returncode == 0, p.stdout[-3000:] + p.stderr[-3000:]
     assert p.stdout.count("gather worker ok") == 2, p.stdout[-2000:]
+
+
+@pytest.mark.parametrize("wtype,k,n,batch,world", [("f16", 1024, 1025, 8, 2), ("f16", 1024, 1025, 8, 3),
+                                                   ("q4_0", 1056, 999, 1, 2), ("f32", 512, 8193, 3, 2)])
+def test_gather_rows_uneven_on_one_gpu(K, O, gpu, wtype, k, n, batch, world):
+    """k200_gather_rows after a plain k200_matmul of each rank's rows: uneven
+    splits (1025 over 2 and 3 ranks, 8193 over 2), batched outputs and a Q4_0
+    shape (K % 256 != 0) the fused GEMV gather declines.  Every rank's buffer
+    must hold the unsharded result bit for bit (same kernels per shard) and
+    match the FP64 gold within the bars of the unsharded tests."""
+    if wtype == "q4_0":
+        wb = _q4(O, k, n, 0x7340D123)
+        t, wt, row_bytes = K.Q4_0, O.WT_Q4_0, k // 32 * 18
+    elif wtype == "f16":
+        wb = O.f16(O.uniform(0x7340D123, n * k, -1.0, 1.0))
+        t, wt, row_bytes = K.F16, O.WT_F16, 2 * k
+    else:
+        wb = O.uniform(0x7340D123, n * k, -1.0, 1.0)
+        t, wt, row_bytes = K.F32, O.WT_F32, 4 * k
+    x = O.uniform(0x09200ABC, k * batch, -1.0, 1.0)
+    raw = np.ascontiguousarray(wb).view(np.uint8).ravel()
+    dw, dx = K.Buffer(0, raw.nbytes), K.Buffer(0, x.nbytes)
+    dw.upload(raw)
+    dx.upload(x)
+    ex = PeerExchange.on_one_device(K, 0, n, world, batch=batch)
+    kern = K.Kernel()
+    shards = []
+    for r in range(world):
+        b, c = row_shard(n, world, r)
+        ys = K.Buffer(0, 4 * c * batch)
+        K.matmul(kern, 0, ys, dw.data() + b * row_bytes, dx, k, c, batch, t)
+        assert K.gather_rows(0, ex[r].view(0), b, ys, c, batch) == 0
+        shards.append(ys)
+    K.select(0)
+    assert K.wait() == 0
+    full = K.Buffer(0, 4 * n * batch)
+    K.matmul(kern, 0, full, dw, dx, k, n, batch, t)
+    K.select(0)
+    K.check(K.wait())
+    whole = full.download(np.float32, n * batch)
+    gold = O.matmul_gold(wb, wt, x, k, n, batch)
+    bar = 1e-3 if (wtype == "f16" and batch >= 4) else 1e-5
+    for r in range(world):
+        got = _download(K, ex[r].output(0), n * batch)
+        assert np.array_equal(got.view(np.uint32), whole.view(np.uint32)), f"rank {r}"
+        assert (_flags(K, ex[r], world) == 1).all()
+    assert (np.abs(whole - gold) <= bar * (1 + np.abs(gold))).all()
+    kern.close()
+    for e in reversed(ex):
+        e.close()

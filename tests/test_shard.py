@@ -124,7 +124,7 @@ def _ranks_over_gloo(rank, world, port, out):
             pass
 
     K = _FakeK()
-    PeerExchange._region = classmethod(lambda cls, K_, dev, n, buffers: Buf(0x10000 * (rank + 1)))
+    PeerExchange._region = classmethod(lambda cls, K_, dev, n, buffers, batch=1: Buf(0x10000 * (rank + 1)))
 
     def all_gather(obj):
         got = [None] * world
