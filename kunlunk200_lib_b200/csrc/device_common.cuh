@@ -75,6 +75,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
     return false;
 }
 
+// The same bounded wait for a thread whose wait is not on the critical path
+// (a producer with many stages of slack): between tests it sleeps `sleep_ns`,
+// so a long wait does not take issue slots from the warps that do the work.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, int *err, int code,
+                                                unsigned sleep_ns) {
+    for (uint32_t i = 0; i < kWaitBudget; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        __nanosleep(sleep_ns);
+    }
+    if (err) atomicExch(err, code);
+    return false;
+}
+
 // 1-D bulk copy global -> shared, completion counted on `bar` in bytes.
 // dst, src and bytes must be multiples of 16.
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {

@@ -89,7 +89,88 @@ struct TcArgs {
     int ksteps;
     uint32_t tmem_cols;      // allocated tensor-memory columns (power of two >= 32)
     int raw_slots;           // q4: raw weight boxes in flight
+    // Persistent schedule over the (tile, chunk) space, chunk = kChunkSteps K
+    // steps: CTA c takes iterations [c * iters / grid, (c + 1) * iters / grid).
+    // Tile t is row tile t / ncolt, column tile t % ncolt.  With grid = tiles
+    // every CTA owns one whole tile; with grid = the SM count (stream-K) a tile
+    // can be split between consecutive CTAs, whose partial accumulators go to
+    // `partials` (two slots per CTA: its first and its last tile) and are
+    // summed in CTA order by the CTA that arrives last (`counters`, zero
+    // between launches).
+    long long iters;
+    int grid, chunks, ncolt;
+    int *counters;
+    void *partials;
 };
+
+constexpr int kChunkSteps = 4;  // K steps per schedule iteration (and per f16/q4 tensor-memory chunk)
+
+// One CTA's run of chunks inside one tile.
+struct Seg {
+    int t, mt, nt;    // tile, its row tile and column tile
+    int ks0, ks1;     // K steps [ks0, ks1)
+    bool whole;       // the CTA computes the whole tile
+    int slot;         // partial slot when not whole
+};
+
+__device__ __forceinline__ long long sk_begin(const TcArgs &a, int cta) { return cta * a.iters / a.grid; }
+// CTA whose range holds iteration it
+__device__ __forceinline__ int sk_owner(const TcArgs &a, long long it) {
+    return static_cast<int>(((it + 1) * a.grid - 1) / a.iters);
+}
+// Partial slot of CTA c's segment of tile t: slot 0 for its first tile, 1 for its last.
+__device__ __forceinline__ int sk_slot(const TcArgs &a, int c, int t) {
+    return 2 * c + (t == static_cast<int>(sk_begin(a, c) / a.chunks) ? 0 : 1);
+}
+
+struct SkWalk {
+    long long i, i1;
+    __device__ explicit SkWalk(const TcArgs &a) : i(sk_begin(a, blockIdx.x)), i1(sk_begin(a, blockIdx.x + 1)) {}
+    __device__ bool next(const TcArgs &a, Seg &s) {
+        if (i >= i1) return false;
+        const long long t = i / a.chunks;
+        const long long e = min(i1, (t + 1) * a.chunks);
+        const int ca = static_cast<int>(i - t * a.chunks), cb = static_cast<int>(e - t * a.chunks);
+        s.t = static_cast<int>(t);
+        s.mt = s.t / a.ncolt;
+        s.nt = s.t - s.mt * a.ncolt;
+        s.ks0 = ca * kChunkSteps;
+        s.ks1 = min(a.ksteps, cb * kChunkSteps);
+        s.whole = ca == 0 && cb == a.chunks;
+        s.slot = sk_slot(a, blockIdx.x, s.t);
+        i = e;
+        return true;
+    }
+};
+
+// The four epilogue warps (2..5) meet here.
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// After this CTA's epilogue threads stored their partials of a split tile:
+// counts the segment in and returns true in every epilogue thread of the CTA
+// that arrived last (it then owns the tile's final sum; the count is reset).
+// Every epilogue thread calls it for every split segment, also after a wait
+// that ran out (ok false: nothing is counted), so the named barriers always
+// meet.
+__device__ __forceinline__ bool sk_arrive(const TcArgs &a, const Seg &s, int *flag, bool ok) {
+    __threadfence();  // this thread's partial stores before the count (device scope)
+    epi_sync();
+    if (threadIdx.x == 64) *flag = 0;
+    if (threadIdx.x == 64 && ok) {
+        const long long it0 = static_cast<long long>(s.t) * a.chunks;
+        const int nseg = sk_owner(a, it0 + a.chunks - 1) - sk_owner(a, it0) + 1;
+        __threadfence();
+        const int prev = atomicAdd(a.counters + s.t, 1);
+        const int last = prev + 1 == nseg;
+        if (last) {
+            __threadfence();
+            a.counters[s.t] = 0;
+        }
+        *flag = last;
+    }
+    epi_sync();
+    return *flag != 0;
+}
 
 // ---- tcgen05 primitives ----------------------------------------------------
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -167,7 +248,10 @@ __device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap *map, int
         : "memory");
 }
 
-// ---- the kernel --------------------------------------------------------------
+// ---- rowwise int8 --------------------------------------------------------------
+// Accumulators of one segment: p0 = W . q0 in columns [0, nb), p1 = W . q1 in
+// [nb, 2 nb).  The next segment's first MMA waits until the epilogue has
+// read them (accfree).
 __global__ void __launch_bounds__(kThreadsTc, 1) gemm_i8_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte aligned stages: [A 128 x 128 B][B0 nb x 128 B][B1 nb x 128 B]
@@ -177,11 +261,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1) gemm_i8_kernel(const __grid_con
     const uint32_t stage_bytes = a_bytes + 2 * b_bytes;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + a.stages * stage_bytes);
     uint64_t *empty = full + a.stages;
-    uint64_t *accum = empty + a.stages;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum + 1);
+    uint64_t *accum = empty + a.stages;  // a segment's accumulators are final
+    uint64_t *accfree = accum + 1;       // the epilogue has read them (4 arrivals)
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accfree + 1);
+    int *flag = reinterpret_cast<int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * kTileM, n0 = blockIdx.y * a.nb;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < a.stages; ++s) {
@@ -189,6 +274,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) gemm_i8_kernel(const __grid_con
             mbar_init(&empty[s], 1);
         }
         mbar_init(accum, 1);
+        mbar_init(accfree, 4);
         fence_mbar_init();
     }
     if (warp == 1) tmem_alloc(tmem_slot, a.tmem_cols);
@@ -201,14 +287,25 @@ __global__ void __launch_bounds__(kThreadsTc, 1) gemm_i8_kernel(const __grid_con
         // ---------------- TMA producer ----------------
         if (lane == 0) {
             pdl_wait_prior();
-            for (int ks = 0; ks < a.ksteps; ++ks) {
-                const int s = ks % a.stages;
-                if (ks >= a.stages && !mbar_wait(&empty[s], ((ks / a.stages) - 1) & 1, a.err, kErrBulkTimeout)) break;
-                const uint32_t st = base + s * stage_bytes;
-                mbar_arrive_expect_tx(&full[s], stage_bytes);
-                tma_2d(st, &maps.a, ks * kStepBytes, m0, &full[s]);
-                tma_2d(st + a_bytes, &maps.b0, ks * kStepBytes, n0, &full[s]);
-                tma_2d(st + a_bytes + b_bytes, &maps.b1, ks * kStepBytes, n0, &full[s]);
+            SkWalk walk(a);
+            Seg sg;
+            int g = 0;  // K steps issued by this CTA (ring position)
+            bool ok = true;
+            while (ok && walk.next(a, sg)) {
+                const int m0 = sg.mt * kTileM, n0 = sg.nt * a.nb;
+                for (int ks = sg.ks0; ks < sg.ks1; ++ks, ++g) {
+                    const int s = g % a.stages;
+                    if (g >= a.stages &&
+                        !mbar_wait_sleep(&empty[s], ((g / a.stages) - 1) & 1, a.err, kErrBulkTimeout, 64)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t st = base + s * stage_bytes;
+                    mbar_arrive_expect_tx(&full[s], stage_bytes);
+                    tma_2d(st, &maps.a, ks * kStepBytes, m0, &full[s]);
+                    tma_2d(st + a_bytes, &maps.b0, ks * kStepBytes, n0, &full[s]);
+                    tma_2d(st + a_bytes + b_bytes, &maps.b1, ks * kStepBytes, n0, &full[s]);
+                }
             }
         }
         __syncwarp();
@@ -219,52 +316,119 @@ __global__ void __launch_bounds__(kThreadsTc, 1) gemm_i8_kernel(const __grid_con
             // the two activation components are adjacent nb-row tiles: one 2nb-wide MMA when it fits
             const bool merged = 2 * a.nb <= 256;
             const uint32_t idesc2 = instr_desc(2, 1, 1, kTileM, merged ? 2 * a.nb : a.nb);
-            for (int ks = 0; ks < a.ksteps; ++ks) {
-                const int s = ks % a.stages;
-                if (!mbar_wait(&full[s], (ks / a.stages) & 1, a.err, kErrBulkTimeout)) break;
+            SkWalk walk(a);
+            Seg sg;
+            int g = 0, seg = 0;
+            bool ok = true;
+            while (ok && walk.next(a, sg)) {
+                if (seg > 0 && !mbar_wait(accfree, (seg - 1) & 1, a.err, kErrMmaTimeout)) break;
                 tc_fence_after();
-                const uint32_t st = base + s * stage_bytes;
-                const uint64_t da = sw128_desc(st), db0 = sw128_desc(st + a_bytes), db1 = sw128_desc(st + a_bytes + b_bytes);
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {  // 4 x 32 bytes of K per 128-byte step: +2 in the address field
-                    const uint32_t acc = (ks | kk) != 0;
-                    if (merged) {
-                        mma_i8(taddr, da + 2 * kk, db0 + 2 * kk, idesc2, acc);
-                    } else {
-                        mma_i8(taddr, da + 2 * kk, db0 + 2 * kk, idesc, acc);
-                        mma_i8(taddr + a.nb, da + 2 * kk, db1 + 2 * kk, idesc, acc);
+                for (int ks = sg.ks0; ks < sg.ks1; ++ks, ++g) {
+                    const int s = g % a.stages;
+                    if (!mbar_wait(&full[s], (g / a.stages) & 1, a.err, kErrBulkTimeout)) {
+                        ok = false;
+                        break;
                     }
+                    tc_fence_after();
+                    const uint32_t st = base + s * stage_bytes;
+                    const uint64_t da = sw128_desc(st), db0 = sw128_desc(st + a_bytes),
+                                   db1 = sw128_desc(st + a_bytes + b_bytes);
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {  // 4 x 32 bytes of K per 128-byte step: +2 in the address field
+                        const uint32_t acc = (ks != sg.ks0) || kk != 0;
+                        if (merged) {
+                            mma_i8(taddr, da + 2 * kk, db0 + 2 * kk, idesc2, acc);
+                        } else {
+                            mma_i8(taddr, da + 2 * kk, db0 + 2 * kk, idesc, acc);
+                            mma_i8(taddr + a.nb, da + 2 * kk, db1 + 2 * kk, idesc, acc);
+                        }
+                    }
+                    mma_commit(&empty[s]);  // frees the stage once these MMAs have read it
                 }
-                mma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+                mma_commit(accum);
+                ++seg;
             }
-            mma_commit(accum);
         }
         __syncwarp();
     } else {
         // ---------------- epilogue: warps 2..5 -> TMEM lane quarters 2,3,0,1 ----------------
         const int quarter = warp & 3;
-        const int row = m0 + quarter * 32 + lane;  // weight row of this thread
-        const bool ok = mbar_wait(accum, 0, a.err, kErrMmaTimeout);
-        tc_fence_after();
-        if (ok) {
-            const uint32_t lane_addr = taddr + (static_cast<uint32_t>(quarter * 32) << 16);
-            const float s0 = __fdiv_rn(a.act_max[0], 127.0f), s1 = __fdiv_rn(a.act_max[1], 127.0f);
+        const int rt = quarter * 32 + lane;  // row of the tile
+        const uint32_t lane_addr = taddr + (static_cast<uint32_t>(quarter * 32) << 16);
+        const float s0 = __fdiv_rn(a.act_max[0], 127.0f), s1 = __fdiv_rn(a.act_max[1], 127.0f);
+        SkWalk walk(a);
+        Seg sg;
+        int seg = 0;
+        bool ok = true;  // false once a wait ran out: the rest only keeps the barriers in step
+        while (walk.next(a, sg)) {
+            ok = __all_sync(0xffffffffu, ok && mbar_wait_sleep(accum, seg & 1, a.err, kErrMmaTimeout, 128));
+            tc_fence_after();
+            const int row = sg.mt * kTileM + rt, n0 = sg.nt * a.nb;
             const float rs = row < a.n ? a.row_scale[row] : 0.f;
-            for (int c0 = 0; c0 < a.nb; c0 += 16) {
+            int *part = static_cast<int *>(a.partials) + static_cast<size_t>(sg.slot) * 2 * a.nb * kTileM + rt;
+            for (int c0 = 0; ok && c0 < a.nb; c0 += 16) {
                 uint32_t p0[16], p1[16];
                 tmem_ld16(lane_addr + c0, p0);
                 tmem_ld16(lane_addr + a.nb + c0, p1);
                 tmem_ld_wait();
+                if (sg.whole) {
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int col = n0 + c0 + i;
-                    if (row < a.n && col < a.batch) {
-                        const float t0 = __fmul_rn(static_cast<float>(static_cast<int>(p0[i])), s0);
-                        const float t1 = __fmul_rn(static_cast<float>(static_cast<int>(p1[i])), s1);
-                        a.y[static_cast<long long>(col) * a.y_stride + row] = __fmul_rn(__fadd_rn(t0, t1), rs);
+                    for (int i = 0; i < 16; ++i) {
+                        const int col = n0 + c0 + i;
+                        if (row < a.n && col < a.batch) {
+                            const float t0 = __fmul_rn(static_cast<float>(static_cast<int>(p0[i])), s0);
+                            const float t1 = __fmul_rn(static_cast<float>(static_cast<int>(p1[i])), s1);
+                            a.y[static_cast<long long>(col) * a.y_stride + row] = __fmul_rn(__fadd_rn(t0, t1), rs);
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        part[(c0 + i) * kTileM] = static_cast<int>(p0[i]);
+                        part[(a.nb + c0 + i) * kTileM] = static_cast<int>(p1[i]);
                     }
                 }
             }
+            // the accumulators are in registers or memory: the next segment may overwrite them
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(accfree);
+            if (!sg.whole && sk_arrive(a, sg, flag, ok)) {
+                // the exact int32 sums of every CTA's segment (CTA order), then the combine;
+                // 16 columns at a time so that the loads of a group are in flight together
+                const long long it0 = static_cast<long long>(sg.t) * a.chunks;
+                const int c_first = sk_owner(a, it0), c_last = sk_owner(a, it0 + a.chunks - 1);
+                for (int c0 = 0; c0 < a.nb; c0 += 16) {
+                    int q0[16], q1[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) q0[i] = q1[i] = 0;
+                    for (int c = c_first; c <= c_last; ++c) {
+                        const int *pp = static_cast<const int *>(a.partials) +
+                                        static_cast<size_t>(sk_slot(a, c, sg.t)) * 2 * a.nb * kTileM + rt;
+                        int v0[16], v1[16];
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            v0[i] = __ldcg(pp + (c0 + i) * kTileM);
+                            v1[i] = __ldcg(pp + (a.nb + c0 + i) * kTileM);
+                        }
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            q0[i] += v0[i];
+                            q1[i] += v1[i];
+                        }
+                    }
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const int col = n0 + c0 + i;
+                        if (row < a.n && col < a.batch) {
+                            const float t0 = __fmul_rn(static_cast<float>(q0[i]), s0);
+                            const float t1 = __fmul_rn(static_cast<float>(q1[i]), s1);
+                            a.y[static_cast<long long>(col) * a.y_stride + row] = __fmul_rn(__fadd_rn(t0, t1), rs);
+                        }
+                    }
+                }
+            }
+            ++seg;
         }
     }
     tc_fence_before();
@@ -276,7 +440,95 @@ __global__ void __launch_bounds__(kThreadsTc, 1) gemm_i8_kernel(const __grid_con
 }
 
 // f16 weights, chunked accumulation; NB activation columns per CTA.
-constexpr int kChunkSteps = 4;
+// Epilogue of the f16 and q4 kernels for one finished segment: sum[] holds
+// the f32 sums of its chunks for this thread's row rt.  A whole tile is
+// written (times each column's 2^e); a split one goes to the partial slot,
+// and the CTA that completes the tile adds every segment's partial in CTA
+// order and writes it.  sum[] is left zero.
+template <int NB>
+__device__ __forceinline__ void f32_segment_out(const TcArgs &a, const Seg &sg, int rt, float (&sum)[NB], int *flag,
+                                                bool ok) {
+    const int row = sg.mt * kTileM + rt, n0 = sg.nt * NB;
+    if (sg.whole) {
+        if (ok && row < a.n) {
+#pragma unroll
+            for (int i = 0; i < NB; ++i) {
+                const int col = n0 + i;
+                if (col < a.batch) a.y[static_cast<long long>(col) * a.y_stride + row] = __fmul_rn(sum[i], a.col_scale[col]);
+            }
+        }
+    } else {
+        float *part = static_cast<float *>(a.partials) + static_cast<size_t>(sg.slot) * NB * kTileM + rt;
+        if (ok) {
+#pragma unroll
+            for (int i = 0; i < NB; ++i) part[i * kTileM] = sum[i];
+        }
+        if (sk_arrive(a, sg, flag, ok)) {
+            const long long it0 = static_cast<long long>(sg.t) * a.chunks;
+            const int c_first = sk_owner(a, it0), c_last = sk_owner(a, it0 + a.chunks - 1);
+#pragma unroll
+            for (int i = 0; i < NB; ++i) sum[i] = 0.f;
+            for (int c = c_first; c <= c_last; ++c) {
+                const float *pp = static_cast<const float *>(a.partials) +
+                                  static_cast<size_t>(sk_slot(a, c, sg.t)) * NB * kTileM + rt;
+#pragma unroll
+                for (int i = 0; i < NB; ++i) sum[i] = __fadd_rn(sum[i], __ldcg(pp + i * kTileM));
+            }
+            if (row < a.n) {
+#pragma unroll
+                for (int i = 0; i < NB; ++i) {
+                    const int col = n0 + i;
+                    if (col < a.batch)
+                        a.y[static_cast<long long>(col) * a.y_stride + row] = __fmul_rn(sum[i], a.col_scale[col]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < NB; ++i) sum[i] = 0.f;
+}
+
+// Epilogue warps of the f16 and q4 kernels: drain every finished chunk of
+// the two tensor-memory slots into sum[] and close each segment.
+template <int NB>
+__device__ __forceinline__ void f32_chunk_epilogue(const TcArgs &a, uint32_t taddr, uint64_t *tfull, uint64_t *tfree,
+                                                   int *flag) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int quarter = warp & 3;
+    const int rt = quarter * 32 + lane;
+    const uint32_t lane_addr = taddr + (static_cast<uint32_t>(quarter * 32) << 16);
+    float sum[NB];
+#pragma unroll
+    for (int i = 0; i < NB; ++i) sum[i] = 0.f;
+    bool ok = true;  // false once a wait ran out: the rest only keeps the barriers in step
+    SkWalk walk(a);
+    Seg sg;
+    int gc = 0;  // chunks drained by this CTA (slot and phase)
+    while (walk.next(a, sg)) {
+        const int nch = (sg.ks1 - sg.ks0 + kChunkSteps - 1) / kChunkSteps;
+        for (int c = 0; c < nch; ++c, ++gc) {
+            const int slot = gc & 1;
+            ok = __all_sync(0xffffffffu, ok && mbar_wait_sleep(&tfull[slot], (gc >> 1) & 1, a.err, kErrMmaTimeout, 32));
+            tc_fence_after();
+            if (ok) {
+#pragma unroll
+                for (int c0 = 0; c0 < 2 * NB; c0 += 16) {
+                    uint32_t p[16];
+                    tmem_ld16(lane_addr + slot * 2 * NB + c0, p);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int i = 0; i < 16; ++i)
+                        sum[(c0 % NB) + i] = __fadd_rn(sum[(c0 % NB) + i], __uint_as_float(p[i]));
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tfree[slot]);
+        }
+        f32_segment_out<NB>(a, sg, rt, sum, flag, ok);
+    }
+}
+
 template <int NB>
 __global__ void __launch_bounds__(kThreadsTc, 1) gemm_f16_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -291,10 +543,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1) gemm_f16_kernel(const __grid_co
     uint64_t *tfull = empty + a.stages;  // [2] a tensor-memory slot holds a finished chunk
     uint64_t *tfree = tfull + 2;         // [2] the epilogue has read a slot
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tfree + 2);
+    int *flag = reinterpret_cast<int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * kTileM, n0 = blockIdx.y * NB;
-    const int nchunks = (a.ksteps + kChunkSteps - 1) / kChunkSteps;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < a.stages; ++s) {
@@ -316,14 +567,25 @@ __global__ void __launch_bounds__(kThreadsTc, 1) gemm_f16_kernel(const __grid_co
     if (warp == 0) {
         if (lane == 0) {
             pdl_wait_prior();
-            for (int ks = 0; ks < a.ksteps; ++ks) {
-                const int s = ks % a.stages;
-                if (ks >= a.stages && !mbar_wait(&empty[s], ((ks / a.stages) - 1) & 1, a.err, kErrBulkTimeout)) break;
-                const uint32_t st = base + s * stage_bytes;
-                mbar_arrive_expect_tx(&full[s], stage_bytes);
-                tma_2d(st, &maps.a, ks * kStepBytes, m0, &full[s]);
-                tma_2d(st + a_total, &maps.b0, ks * kStepBytes, n0, &full[s]);
-                tma_2d(st + a_total + b_bytes, &maps.b1, ks * kStepBytes, n0, &full[s]);
+            SkWalk walk(a);
+            Seg sg;
+            int g = 0;
+            bool ok = true;
+            while (ok && walk.next(a, sg)) {
+                const int m0 = sg.mt * kTileM, n0 = sg.nt * NB;
+                for (int ks = sg.ks0; ks < sg.ks1; ++ks, ++g) {
+                    const int s = g % a.stages;
+                    if (g >= a.stages &&
+                        !mbar_wait_sleep(&empty[s], ((g / a.stages) - 1) & 1, a.err, kErrBulkTimeout, 64)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t st = base + s * stage_bytes;
+                    mbar_arrive_expect_tx(&full[s], stage_bytes);
+                    tma_2d(st, &maps.a, ks * kStepBytes, m0, &full[s]);
+                    tma_2d(st + a_total, &maps.b0, ks * kStepBytes, n0, &full[s]);
+                    tma_2d(st + a_total + b_bytes, &maps.b1, ks * kStepBytes, n0, &full[s]);
+                }
             }
         }
         __syncwarp();
@@ -331,60 +593,41 @@ __global__ void __launch_bounds__(kThreadsTc, 1) gemm_f16_kernel(const __grid_co
         if (lane == 0) {
             // f32 <- f16 x f16; x hi and x lo are adjacent NB-row tiles: one 2NB-wide MMA
             const uint32_t idesc = instr_desc(1, 0, 0, kTileM, 2 * NB);
+            SkWalk walk(a);
+            Seg sg;
+            int g = 0, gc = 0;
             bool ok = true;
-            for (int c = 0; c < nchunks && ok; ++c) {
-                const int slot = c & 1;
-                if (c >= 2 && !mbar_wait(&tfree[slot], ((c >> 1) - 1) & 1, a.err, kErrMmaTimeout)) break;
-                tc_fence_after();
-                const uint32_t d = taddr + slot * 2 * NB;  // [W*x hi | W*x lo]
-                const int ks_end = min(a.ksteps, (c + 1) * kChunkSteps);
-                for (int ks = c * kChunkSteps; ks < ks_end; ++ks) {
-                    const int s = ks % a.stages;
-                    if (!mbar_wait(&full[s], (ks / a.stages) & 1, a.err, kErrBulkTimeout)) { ok = false; break; }
+            while (ok && walk.next(a, sg)) {
+                for (int c0 = sg.ks0; ok && c0 < sg.ks1; c0 += kChunkSteps, ++gc) {
+                    const int slot = gc & 1;
+                    if (gc >= 2 && !mbar_wait(&tfree[slot], ((gc >> 1) - 1) & 1, a.err, kErrMmaTimeout)) {
+                        ok = false;
+                        break;
+                    }
                     tc_fence_after();
-                    const uint32_t st = base + s * stage_bytes;
-                    const uint64_t da = sw128_desc(st);
-                    const uint64_t db = sw128_desc(st + a_total);
+                    const uint32_t d = taddr + slot * 2 * NB;  // [W*x hi | W*x lo]
+                    const int ks_end = min(sg.ks1, c0 + kChunkSteps);
+                    for (int ks = c0; ks < ks_end; ++ks, ++g) {
+                        const int s = g % a.stages;
+                        if (!mbar_wait(&full[s], (g / a.stages) & 1, a.err, kErrBulkTimeout)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t st = base + s * stage_bytes;
+                        const uint64_t da = sw128_desc(st);
+                        const uint64_t db = sw128_desc(st + a_total);
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        mma_f16(d, da + 2 * kk, db + 2 * kk, idesc, (ks != c * kChunkSteps) || kk != 0);
-                    mma_commit(&empty[s]);
+                        for (int kk = 0; kk < 4; ++kk) mma_f16(d, da + 2 * kk, db + 2 * kk, idesc, (ks != c0) || kk != 0);
+                        mma_commit(&empty[s]);
+                    }
+                    mma_commit(&tfull[slot]);
                 }
-                mma_commit(&tfull[slot]);
             }
         }
         __syncwarp();
     } else {
-        const int quarter = warp & 3;
-        const int row = m0 + quarter * 32 + lane;
-        const uint32_t lane_addr = taddr + (static_cast<uint32_t>(quarter * 32) << 16);
-        float sum[NB];
-#pragma unroll
-        for (int i = 0; i < NB; ++i) sum[i] = 0.f;
-        bool ok = true;
-        for (int c = 0; c < nchunks; ++c) {
-            const int slot = c & 1;
-            if (!mbar_wait(&tfull[slot], (c >> 1) & 1, a.err, kErrMmaTimeout)) { ok = false; break; }
-            tc_fence_after();
-#pragma unroll
-            for (int c0 = 0; c0 < 2 * NB; c0 += 16) {
-                uint32_t p[16];
-                tmem_ld16(lane_addr + slot * 2 * NB + c0, p);
-                tmem_ld_wait();
-#pragma unroll
-                for (int i = 0; i < 16; ++i) sum[(c0 % NB) + i] = __fadd_rn(sum[(c0 % NB) + i], __uint_as_float(p[i]));
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tfree[slot]);
-        }
-        if (ok && row < a.n) {
-#pragma unroll
-            for (int i = 0; i < NB; ++i) {
-                const int col = n0 + i;
-                if (col < a.batch) a.y[static_cast<long long>(col) * a.y_stride + row] = __fmul_rn(sum[i], a.col_scale[col]);
-            }
-        }
+        f32_chunk_epilogue<NB>(a, taddr, tfull, tfree, flag);
     }
     tc_fence_before();
     __syncthreads();
@@ -459,12 +702,10 @@ __global__ void __launch_bounds__(kThreadsQ4, 1) gemm_q4_kernel(const __grid_con
     uint64_t *full_r = tfree + 2;         // raw box landed (TMA)
     uint64_t *empty_r = full_r + a.raw_slots;  // raw box read by all 128 dequantisers
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(empty_r + a.raw_slots);
-    const uint32_t raw_u = base + a.stages * stage_bytes + kBarBytesQ4;  // raw ring [slot][row][144 B]
-    const int nbox = (a.ksteps + kRawSteps - 1) / kRawSteps;  // the last box may run past the row (zero fill)
+    int *flag = reinterpret_cast<int *>(tmem_slot + 1);
+    const uint32_t raw_u = base + a.stages * stage_bytes + kBarBytesQ4;  // raw ring [slot][row][288 B]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * kTileM, n0 = blockIdx.y * NB;
-    const int nchunks = (a.ksteps + kChunkSteps - 1) / kChunkSteps;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < a.stages; ++s) {
@@ -490,15 +731,29 @@ __global__ void __launch_bounds__(kThreadsQ4, 1) gemm_q4_kernel(const __grid_con
 
     if (warp == 10) {
         // ---------------- raw weight boxes by TMA ----------------
+        // A segment's K steps [ks0, ks1) are covered by boxes of kRawSteps
+        // steps from ks0 (ks0 is a multiple of four, so a box starts on a
+        // 16-byte boundary: 144 bytes per four steps); the last box may run
+        // past the segment (the dequantisers skip those steps) or past the
+        // row (zero fill).
         if (lane == 0) {
             pdl_wait_prior();
-            for (int rb = 0; rb < nbox; ++rb) {
-                const int rs = rb % a.raw_slots;
-                if (rb >= a.raw_slots &&
-                    !mbar_wait(&empty_r[rs], ((rb / a.raw_slots) - 1) & 1, a.err, kErrBulkTimeout))
-                    break;
-                mbar_arrive_expect_tx(&full_r[rs], kRawBox);
-                tma_2d(raw_u + rs * kRawBox, &maps.a, rb * (kRawRow / 4), m0, &full_r[rs]);
+            SkWalk walk(a);
+            Seg sg;
+            int gr = 0;  // boxes issued by this CTA (raw ring position)
+            bool ok = true;
+            while (ok && walk.next(a, sg)) {
+                const int m0 = sg.mt * kTileM;
+                for (int ks = sg.ks0; ks < sg.ks1; ks += kRawSteps, ++gr) {
+                    const int rs = gr % a.raw_slots;
+                    if (gr >= a.raw_slots &&
+                        !mbar_wait_sleep(&empty_r[rs], ((gr / a.raw_slots) - 1) & 1, a.err, kErrBulkTimeout, 64)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full_r[rs], kRawBox);
+                    tma_2d(raw_u + rs * kRawBox, &maps.a, ks * (kRawRow / kRawSteps / 4), m0, &full_r[rs]);
+                }
             }
         }
         __syncwarp();
@@ -506,13 +761,24 @@ __global__ void __launch_bounds__(kThreadsQ4, 1) gemm_q4_kernel(const __grid_con
         // ---------------- activations by TMA ----------------
         if (lane == 0) {
             pdl_wait_prior();
-            for (int ks = 0; ks < a.ksteps; ++ks) {
-                const int s = ks % a.stages;
-                if (ks >= a.stages && !mbar_wait(&empty[s], ((ks / a.stages) - 1) & 1, a.err, kErrBulkTimeout)) break;
-                const uint32_t st = base + s * stage_bytes;
-                mbar_arrive_expect_tx(&full_x[s], 2 * b_bytes);
-                tma_2d(st + 2 * a_bytes, &maps.b0, ks * kStepBytes, n0, &full_x[s]);
-                tma_2d(st + 2 * a_bytes + b_bytes, &maps.b1, ks * kStepBytes, n0, &full_x[s]);
+            SkWalk walk(a);
+            Seg sg;
+            int g = 0;
+            bool ok = true;
+            while (ok && walk.next(a, sg)) {
+                const int n0 = sg.nt * NB;
+                for (int ks = sg.ks0; ks < sg.ks1; ++ks, ++g) {
+                    const int s = g % a.stages;
+                    if (g >= a.stages &&
+                        !mbar_wait_sleep(&empty[s], ((g / a.stages) - 1) & 1, a.err, kErrBulkTimeout, 64)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t st = base + s * stage_bytes;
+                    mbar_arrive_expect_tx(&full_x[s], 2 * b_bytes);
+                    tma_2d(st + 2 * a_bytes, &maps.b0, ks * kStepBytes, n0, &full_x[s]);
+                    tma_2d(st + 2 * a_bytes + b_bytes, &maps.b1, ks * kStepBytes, n0, &full_x[s]);
+                }
             }
         }
         __syncwarp();
@@ -521,113 +787,105 @@ __global__ void __launch_bounds__(kThreadsQ4, 1) gemm_q4_kernel(const __grid_con
         if (lane == 0) {
             // x hi and x lo are adjacent NB-row tiles: one 2NB-row operand
             const uint32_t idesc2 = instr_desc(1, 0, 0, kTileM, 2 * NB), idesc1 = instr_desc(1, 0, 0, kTileM, NB);
+            SkWalk walk(a);
+            Seg sg;
+            int g = 0, gc = 0;
             bool ok = true;
-            for (int c = 0; c < nchunks && ok; ++c) {
-                const int slot = c & 1;
-                if (c >= 2 && !mbar_wait(&tfree[slot], ((c >> 1) - 1) & 1, a.err, kErrMmaTimeout)) break;
-                tc_fence_after();
-                const uint32_t d = taddr + slot * 2 * NB;  // [W*x hi | W hi*x lo]
-                const int ks_end = min(a.ksteps, (c + 1) * kChunkSteps);
-                for (int ks = c * kChunkSteps; ks < ks_end; ++ks) {
-                    const int s = ks % a.stages;
-                    const uint32_t par = (ks / a.stages) & 1;
-                    if (!mbar_wait(&full_x[s], par, a.err, kErrBulkTimeout) ||
-                        !mbar_wait(&full_w[s], par, a.err, kErrBulkTimeout)) { ok = false; break; }
-                    tc_fence_after();
-                    const uint32_t st = base + s * stage_bytes;
-                    const uint64_t dh = sw128_desc(st), dl = sw128_desc(st + a_bytes);
-                    const uint64_t xh = sw128_desc(st + 2 * a_bytes);
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {
-                        mma_f16(d, dh + 2 * kk, xh + 2 * kk, idesc2, (ks != c * kChunkSteps) || kk != 0);
-                        mma_f16(d, dl + 2 * kk, xh + 2 * kk, idesc1, 1);
+            while (ok && walk.next(a, sg)) {
+                for (int c0 = sg.ks0; ok && c0 < sg.ks1; c0 += kChunkSteps, ++gc) {
+                    const int slot = gc & 1;
+                    if (gc >= 2 && !mbar_wait(&tfree[slot], ((gc >> 1) - 1) & 1, a.err, kErrMmaTimeout)) {
+                        ok = false;
+                        break;
                     }
-                    mma_commit(&empty[s]);
+                    tc_fence_after();
+                    const uint32_t d = taddr + slot * 2 * NB;  // [W*x hi | W hi*x lo]
+                    const int ks_end = min(sg.ks1, c0 + kChunkSteps);
+                    for (int ks = c0; ks < ks_end; ++ks, ++g) {
+                        const int s = g % a.stages;
+                        const uint32_t par = (g / a.stages) & 1;
+                        if (!mbar_wait(&full_x[s], par, a.err, kErrBulkTimeout) ||
+                            !mbar_wait(&full_w[s], par, a.err, kErrBulkTimeout)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t st = base + s * stage_bytes;
+                        const uint64_t dh = sw128_desc(st), dl = sw128_desc(st + a_bytes);
+                        const uint64_t xh = sw128_desc(st + 2 * a_bytes);
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk) {
+                            mma_f16(d, dh + 2 * kk, xh + 2 * kk, idesc2, (ks != c0) || kk != 0);
+                            mma_f16(d, dl + 2 * kk, xh + 2 * kk, idesc1, 1);
+                        }
+                        mma_commit(&empty[s]);
+                    }
+                    mma_commit(&tfull[slot]);
                 }
-                mma_commit(&tfull[slot]);
             }
         }
         __syncwarp();
     } else if (warp < 6) {
         // ---------------- epilogue: chunk sums in f32 registers ----------------
-        const int quarter = warp & 3;
-        const int row = m0 + quarter * 32 + lane;
-        const uint32_t lane_addr = taddr + (static_cast<uint32_t>(quarter * 32) << 16);
-        float sum[NB];
-#pragma unroll
-        for (int i = 0; i < NB; ++i) sum[i] = 0.f;
-        bool ok = true;
-        for (int c = 0; c < nchunks; ++c) {
-            const int slot = c & 1;
-            if (!mbar_wait(&tfull[slot], (c >> 1) & 1, a.err, kErrMmaTimeout)) { ok = false; break; }
-            tc_fence_after();
-#pragma unroll
-            for (int c0 = 0; c0 < 2 * NB; c0 += 16) {
-                uint32_t p[16];
-                tmem_ld16(lane_addr + slot * 2 * NB + c0, p);
-                tmem_ld_wait();
-#pragma unroll
-                for (int i = 0; i < 16; ++i) sum[(c0 % NB) + i] = __fadd_rn(sum[(c0 % NB) + i], __uint_as_float(p[i]));
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tfree[slot]);
-        }
-        if (ok && row < a.n) {
-#pragma unroll
-            for (int i = 0; i < NB; ++i) {
-                const int col = n0 + i;
-                if (col < a.batch) a.y[static_cast<long long>(col) * a.y_stride + row] = __fmul_rn(sum[i], a.col_scale[col]);
-            }
-        }
+        f32_chunk_epilogue<NB>(a, taddr, tfull, tfree, flag);
     } else {
         // ---------------- dequantisers: one weight row per thread ----------------
         const int rt = threadIdx.x - 192;  // row in the tile
         const uint32_t row_off = (rt >> 3) * 1024 + (rt & 7) * 128;  // swizzled tile row
         const uint32_t sw = rt & 7;
+        SkWalk walk(a);
+        Seg sg;
+        int g = 0, gr = 0;
         bool ok = true;
-        for (int rb = 0; rb < nbox && ok; ++rb) {
-            const int rs = rb % a.raw_slots;
-            if (!mbar_wait(&full_r[rs], (rb / a.raw_slots) & 1, a.err, kErrBulkTimeout)) break;
-#pragma unroll
-            for (int half = 0; half < kRawSteps / 4 && ok; ++half) {
-                uint32_t w[36];  // four K steps of this row: per step two blocks (2-byte scale + 16 nibble bytes)
-                const uint32_t rp = raw_u + rs * kRawBox + rt * kRawRow + half * 144;
-#pragma unroll
-                for (int c = 0; c < 9; ++c)
-                    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                                 : "=r"(w[4 * c]), "=r"(w[4 * c + 1]), "=r"(w[4 * c + 2]), "=r"(w[4 * c + 3])
-                                 : "r"(rp + 16 * c));
-                if (half == kRawSteps / 4 - 1) {
-                    // order these generic reads before the copy engine's next write into the slot
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    mbar_arrive(&empty_r[rs]);
+        while (ok && walk.next(a, sg)) {
+            for (int kb = sg.ks0; ok && kb < sg.ks1; kb += kRawSteps, ++gr) {
+                const int rs = gr % a.raw_slots;
+                if (!mbar_wait(&full_r[rs], (gr / a.raw_slots) & 1, a.err, kErrBulkTimeout)) {
+                    ok = false;
+                    break;
                 }
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int ks = rb * kRawSteps + half * 4 + j;
-                    if (ks >= a.ksteps) break;
-                    const int s = ks % a.stages;
-                    if (ks >= a.stages && !mbar_wait(&empty[s], ((ks / a.stages) - 1) & 1, a.err, kErrBulkTimeout)) {
-                        ok = false;
-                        break;
-                    }
-                    const uint32_t th = base + s * stage_bytes + row_off, tl = th + a_bytes;
-                    const uint32_t *v = w + 9 * j;
-                    // block 0: scale in bytes 0-1, nibbles in bytes 2-17; block 1: scale 18-19, nibbles 20-35
-                    const uint32_t d0 = __byte_perm(v[0], v[0], 0x1010), d1 = __byte_perm(v[4], v[4], 0x3232);
+                for (int half = 0; half < kRawSteps / 4; ++half) {
+                    uint32_t w[36];  // four K steps of this row: per step two blocks (2-byte scale + 16 nibble bytes)
+                    const uint32_t rp = raw_u + rs * kRawBox + rt * kRawRow + half * 144;
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        uint4 h, l;
-                        q4_chunk(__byte_perm(v[q], v[q + 1], 0x5432), d0, h, l);
-                        sts128(th + ((q ^ sw) << 4), h);
-                        sts128(tl + ((q ^ sw) << 4), l);
-                        q4_chunk(v[5 + q], d1, h, l);
-                        sts128(th + (((4 + q) ^ sw) << 4), h);
-                        sts128(tl + (((4 + q) ^ sw) << 4), l);
+                    for (int c = 0; c < 9; ++c)
+                        asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                                     : "=r"(w[4 * c]), "=r"(w[4 * c + 1]), "=r"(w[4 * c + 2]), "=r"(w[4 * c + 3])
+                                     : "r"(rp + 16 * c));
+                    if (half == kRawSteps / 4 - 1) {
+                        // order these generic reads before the copy engine's next write into the slot
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                        mbar_arrive(&empty_r[rs]);
                     }
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> MMA reads
-                    mbar_arrive(&full_w[s]);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int ks = kb + half * 4 + j;
+                        if (!ok || ks >= sg.ks1) break;
+                        const int s = g % a.stages;
+                        if (g >= a.stages &&
+                            !mbar_wait_sleep(&empty[s], ((g / a.stages) - 1) & 1, a.err, kErrBulkTimeout, 64)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t th = base + s * stage_bytes + row_off, tl = th + a_bytes;
+                        const uint32_t *v = w + 9 * j;
+                        // block 0: scale in bytes 0-1, nibbles in bytes 2-17; block 1: scale 18-19, nibbles 20-35
+                        const uint32_t d0 = __byte_perm(v[0], v[0], 0x1010), d1 = __byte_perm(v[4], v[4], 0x3232);
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            uint4 h, l;
+                            q4_chunk(__byte_perm(v[q], v[q + 1], 0x5432), d0, h, l);
+                            sts128(th + ((q ^ sw) << 4), h);
+                            sts128(tl + ((q ^ sw) << 4), l);
+                            q4_chunk(v[5 + q], d1, h, l);
+                            sts128(th + (((4 + q) ^ sw) << 4), h);
+                            sts128(tl + (((4 + q) ^ sw) << 4), l);
+                        }
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> MMA reads
+                        mbar_arrive(&full_w[s]);
+                        ++g;
+                    }
                 }
             }
         }
@@ -731,12 +989,60 @@ bool gemm_tc_supported(int wt, int k, int n, int batch) {
 
 namespace {
 size_t align256(size_t b) { return (b + 255) & ~size_t(255); }
+
+// Tile shape and schedule of one batched matmul.
+struct TcShape {
+    int nb;             // activation columns per tile (MMA N)
+    int ksteps, chunks; // K steps of 128 operand bytes, schedule chunks per tile
+    int tiles, ncolt;
+    long long iters;
+};
+
+TcShape tc_shape(int wt, int k, int n, int batch) {
+    TcShape t{};
+    const bool i8 = wt == 3;
+    const int cap = i8 ? 256 : 128;  // the f16/q4 epilogue keeps NB sums per thread in registers
+    t.nb = batch >= cap ? cap : (batch + 15) / 16 * 16;
+    if (!i8) t.nb = t.nb <= 16 ? 16 : t.nb <= 32 ? 32 : t.nb <= 64 ? 64 : 128;
+    const long long row_bytes = i8 ? k : 2ll * k;  // bytes per row of the MMA operands
+    t.ksteps = static_cast<int>((row_bytes + kStepBytes - 1) / kStepBytes);
+    t.chunks = (t.ksteps + kChunkSteps - 1) / kChunkSteps;
+    t.ncolt = (batch + t.nb - 1) / t.nb;
+    t.tiles = ((n + kTileM - 1) / kTileM) * t.ncolt;
+    t.iters = static_cast<long long>(t.tiles) * t.chunks;
+    return t;
+}
+
+// Stream-K pays when one CTA per tile would leave SMs idle: fewer tiles
+// than SMs, or a last wave that is less than 95% full.  Measured on B200
+// (per-step time, stream-K against one CTA per tile): f16 K8192 N8192 B64
+// 57 vs 78 us, int8 K8192 N28672 B32 75 vs 82 us, B256 174 vs 175 us,
+// q4_0 K4096 N14336 B16 57 vs 59 us; but q4_0 with wide tiles lost (B128
+// 83 vs 70 us, B512 254 vs 249 us: its four dequantiser warps restart their
+// pipeline at every segment and the 64 KB partials do not pay back), so
+// q4_0 takes it only for tiles of at most 32 columns.
+bool tc_stream_k(int wt, const TcShape &t, int sms, bool allowed) {
+    if (!allowed || sms <= 0 || t.tiles % sms == 0) return false;
+    if (wt == 2 && t.nb > 32) return false;
+    const long long waves = (t.tiles + sms - 1) / sms;
+    return t.tiles < sms || static_cast<double>(t.tiles) / static_cast<double>(waves * sms) < 0.95;
+}
+
+size_t tc_partial_slot_bytes(int wt, const TcShape &t) {
+    return static_cast<size_t>(kTileM) * t.nb * 4 * (wt == 3 ? 2 : 1);
+}
 }  // namespace
 
-size_t gemm_tc_scratch_bytes(int wt, int k, int n, int batch) {
-    (void)n;
-    if (wt != 1 && wt != 2) return 0;
-    return 2 * align256(static_cast<size_t>(batch) * k * 2) + align256(static_cast<size_t>(batch) * 4);
+// Scratch of one batched matmul: the f16 hi/lo activation split (f16 and
+// q4_0), then, when the stream-K schedule is used, the per-tile arrival
+// counters (zero) and two partial-accumulator slots per CTA.
+size_t gemm_tc_scratch_bytes(int wt, int k, int n, int batch, const DeviceInfo &dev) {
+    if (wt != 1 && wt != 2 && wt != 3) return 0;
+    size_t bytes = wt == 3 ? 0 : 2 * align256(static_cast<size_t>(batch) * k * 2) + align256(static_cast<size_t>(batch) * 4);
+    const TcShape t = tc_shape(wt, k, n, batch);
+    if (tc_stream_k(wt, t, dev.sm_count, dev.stream_k))
+        bytes += align256(static_cast<size_t>(t.tiles) * 4) + 2 * static_cast<size_t>(dev.sm_count) * tc_partial_slot_bytes(wt, t);
+    return bytes;
 }
 
 cudaError_t launch_gemm_tc(const GemvRequest &r, const DeviceInfo &dev, cudaStream_t stream) {
@@ -746,7 +1052,9 @@ cudaError_t launch_gemm_tc(const GemvRequest &r, const DeviceInfo &dev, cudaStre
     if (q4 && r.k % 256) return cudaErrorNotSupported;  // 16-byte multiple rows
     if (i8 && ((reinterpret_cast<uintptr_t>(r.q) & 15) || (r.q_comp & 15) || r.q_stride != r.k))
         return cudaErrorNotSupported;
-    if (!i8 && (!r.split || r.split_bytes < gemm_tc_scratch_bytes(r.wt, r.k, r.n, r.batch))) return cudaErrorNotSupported;
+    if (!i8 && (!r.split || r.split_bytes < 2 * align256(static_cast<size_t>(r.batch) * r.k * 2) +
+                                               align256(static_cast<size_t>(r.batch) * 4)))
+        return cudaErrorNotSupported;
     TcArgs a{};
     a.w = static_cast<const uint8_t *>(r.w);
     a.row_bytes = static_cast<long long>(r.k / 32) * 18;
@@ -758,11 +1066,25 @@ cudaError_t launch_gemm_tc(const GemvRequest &r, const DeviceInfo &dev, cudaStre
     a.n = r.n;
     a.batch = r.batch;
     a.y_stride = r.y_stride;
-    const int cap = i8 ? 256 : 128;  // the f16/q4 epilogue keeps NB sums per thread in registers
-    a.nb = r.batch >= cap ? cap : (r.batch + 15) / 16 * 16;
-    if (!i8) a.nb = a.nb <= 16 ? 16 : a.nb <= 32 ? 32 : a.nb <= 64 ? 64 : 128;
+    const TcShape shape = tc_shape(r.wt, r.k, r.n, r.batch);
+    a.nb = shape.nb;
     const long long row_bytes = i8 ? r.k : 2ll * r.k;  // bytes per row of the MMA operands
-    a.ksteps = static_cast<int>((row_bytes + kStepBytes - 1) / kStepBytes);
+    a.ksteps = shape.ksteps;
+    a.chunks = shape.chunks;
+    a.ncolt = shape.ncolt;
+    a.iters = shape.iters;
+    // one CTA per tile, or (with the scratch for partials) one per SM over equal shares of the work
+    const size_t act_bytes = i8 ? 0 : 2 * align256(static_cast<size_t>(r.batch) * r.k * 2) + align256(static_cast<size_t>(r.batch) * 4);
+    const bool sk = tc_stream_k(r.wt, shape, dev.sm_count, dev.stream_k) && r.split &&
+                    r.split_bytes >= gemm_tc_scratch_bytes(r.wt, r.k, r.n, r.batch, dev);
+    // (at least one iteration per CTA: then consecutive CTAs start at strictly
+    // increasing iterations, and a tile's segments come from consecutive CTAs)
+    a.grid = sk ? static_cast<int>(shape.iters < dev.sm_count ? shape.iters : dev.sm_count) : shape.tiles;
+    if (sk) {
+        char *sk_base = static_cast<char *>(r.split) + act_bytes;
+        a.counters = reinterpret_cast<int *>(sk_base);
+        a.partials = sk_base + align256(static_cast<size_t>(shape.tiles) * 4);
+    }
     uint32_t cols = 32;
     // i8: two accumulators; f16 and q4: two chunk slots of 2 x nb columns
     while (cols < static_cast<uint32_t>((i8 ? 2 : 4) * a.nb)) cols <<= 1;
@@ -819,7 +1141,7 @@ cudaError_t launch_gemm_tc(const GemvRequest &r, const DeviceInfo &dev, cudaStre
         if (devno >= 0 && devno < 64) configured[ki][devno] = static_cast<int>(smem);
     }
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3((r.n + kTileM - 1) / kTileM, (r.batch + a.nb - 1) / a.nb);
+    cfg.gridDim = dim3(a.grid);
     cfg.blockDim = dim3(q4 ? kThreadsQ4 : kThreadsTc);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;

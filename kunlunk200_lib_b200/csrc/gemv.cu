@@ -454,7 +454,8 @@ __global__ void __maxnreg__((Shape<WT, B>::maxreg)) gemv_stream_kernel(const Gem
             int issued = 0;
             for (int c = 0; c < nchunks; ++c) {
                 const int s = c % a.stages;
-                if (c >= a.stages && !mbar_wait(&empty[s], ((c / a.stages) - 1) & 1, a.err, kErrBulkTimeout)) break;
+                if (c >= a.stages && !mbar_wait_sleep(&empty[s], ((c / a.stages) - 1) & 1, a.err, kErrBulkTimeout, 64))
+                    break;
                 if (c == (a.prefetch < a.stages ? a.prefetch : a.stages)) pdl_wait_prior();
                 const int r0 = row_begin + c * a.chunk_rows;
                 const int rows = min(a.chunk_rows, row_end - r0);
@@ -467,7 +468,7 @@ __global__ void __maxnreg__((Shape<WT, B>::maxreg)) gemv_stream_kernel(const Gem
             if (issued <= (a.prefetch < a.stages ? a.prefetch : a.stages)) pdl_wait_prior();
             // never exit with a bulk copy still writing into this CTA's shared memory
             for (int c = issued > a.stages ? issued - a.stages : 0; c < issued; ++c)
-                (void)mbar_wait(&full[c % a.stages], (c / a.stages) & 1, a.err, kErrBulkTimeout);
+                (void)mbar_wait_sleep(&full[c % a.stages], (c / a.stages) & 1, a.err, kErrBulkTimeout, 64);
         }
         return;
     }

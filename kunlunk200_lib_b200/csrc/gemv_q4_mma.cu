@@ -25,9 +25,9 @@
 //    rows, read as 592 so that the row pitch in shared memory is bank-
 //    conflict-free) and one narrower box for the remainder;
 //  * the ring has 16 stages and box j lands in stage j mod 16.  Unit slot q
-//    of box j goes to consumer warp 4 (j mod 4) + q, so each stage is read by
-//    a fixed quad of warps, each warp meets a stage's phases in order, and
-//    the work per warp is balanced to within about one unit.  A warp
+//    of box j goes to consumer warp 4 (j mod Q) + q (Q quads of warps), so
+//    each warp meets its boxes' phases in order and the work per warp is
+//    balanced to within about one unit.  A warp
 //    computes its unit (one m16 tile per group of four blocks) and releases
 //    its slot with one mbarrier arrival (the producer arrives for the slots a
 //    narrow box lacks).  The producer records each box's position in a small
@@ -78,9 +78,14 @@ __host__ __device__ constexpr int box_words(int w) { return kPairWords * w + ((w
 constexpr int kStageBytes = kTileRows * 4 * box_words(kMaxBoxPairs);  // 9472
 constexpr int kRecBytes = 544;                         // fragment record of one group
 constexpr int kZeroOff = 512, kScaleOff = 528;
-constexpr int kWarps = 16;                             // consumer warps
-constexpr int kStages = kWarps;                        // one ring stage per consumer warp
+#ifndef K200_Q4_GEMV_WARPS
+#define K200_Q4_GEMV_WARPS 16
+#endif
+constexpr int kWarps = K200_Q4_GEMV_WARPS;             // consumer warps, four per box
+constexpr int kQuads = kWarps / 4;                     // box j is read by quad j mod kQuads
+constexpr int kStages = 16;                            // ring stages (box j in stage j mod 16)
 constexpr int kThreads = (kWarps + 1) * 32;
+static_assert(kWarps % 4 == 0 && kWarps >= 16, "consumer warps come in quads, at least one per four stages");
 
 struct Q4MmaArgs {
     const float *x;
@@ -350,7 +355,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             int j = 0;
             for (BoxWalk bw(u0, u1, a.ppr); bw.u < u1 && j < a.max_boxes; bw.next(), ++j) {
                 const int s = j % kStages;
-                if (j >= kStages && !mbar_wait(&empty[s], ((j / kStages) & 1) ^ 1, a.err, kErrBulkTimeout)) break;
+                if (j >= kStages && !mbar_wait_sleep(&empty[s], ((j / kStages) & 1) ^ 1, a.err, kErrBulkTimeout, 128))
+                    break;
                 if (j == early) pdl_wait_prior();
                 // published to the consumer by the arrive below (release) and its wait (acquire)
                 box_tab[j] = static_cast<uint32_t>(bw.tile - t_first) | (static_cast<uint32_t>(bw.pair) << 16) |
@@ -364,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (j <= early) pdl_wait_prior();
             // never exit with a copy still writing into this CTA's shared memory
             for (int i = j > kStages ? j - kStages : 0; i < j; ++i)
-                (void)mbar_wait(&full[i % kStages], (i / kStages) & 1, a.err, kErrBulkTimeout);
+                (void)mbar_wait_sleep(&full[i % kStages], (i / kStages) & 1, a.err, kErrBulkTimeout, 128);
         }
         return;
     }
@@ -379,21 +385,38 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     {
         // fragment records: four threads per activation block; every load of a
-        // thread is issued before the first conversion
-        constexpr int kPasses = 4;  // K <= 16384: at most 2048 slots = 4 passes of 512 threads
-        const int nslots = groups * 16;
+        // thread is issued before the first conversion.  Only the unit pairs
+        // (256-element K ranges, 32 slots each) that this CTA's units touch
+        // are built: the pairs p_first .. ppr-1 and 0 .. p_end-1 of its first
+        // and last row tiles, i.e. every pair once the range covers a whole
+        // row tile.  (K <= 16384: at most 2048 slots.)
+        constexpr int kPasses = (2048 + kWarps * 32 - 1) / (kWarps * 32);
+        const int pf = u0 - t_first * a.ppr, pe = u1 - t_last * a.ppr;
+        int p_start = 0, npairs = a.ppr;
+        if (t_first == t_last) {
+            p_start = pf;
+            npairs = pe - pf;
+        } else if (t_last == t_first + 1 && pe <= pf) {
+            p_start = pf;
+            npairs = a.ppr - pf + pe;
+        }
+        const int count = 32 * npairs;  // a multiple of 32: whole warps are inside or past the range
         float xv[kPasses][8];
 #pragma unroll
         for (int k = 0; k < kPasses; ++k)
-            if (k * kWarps * 32 < nslots) {
-                const int b = min(k * kWarps * 32 + tid, nslots - 1) >> 2;
+            if (k * kWarps * 32 < count) {
+                const int t = min(k * kWarps * 32 + tid, count - 1);
+                const int pr = p_start + (t >> 5);
+                const int b = ((pr < a.ppr ? pr : pr - a.ppr) * 32 + (t & 31)) >> 2;
                 load_slot(a.x + 32 * b, b & 3, lane & 3, xv[k], peer_x);
             }
 #pragma unroll
         for (int k = 0; k < kPasses; ++k)
-            if (k * kWarps * 32 < nslots) {
-                const int t = k * kWarps * 32 + tid, b = min(t, nslots - 1) >> 2;
-                store_slot(xv[k], xrec + (b >> 2) * kRecBytes, b & 3, lane & 3, t < nslots);
+            if (k * kWarps * 32 < count) {
+                const int t0 = k * kWarps * 32 + tid, t = min(t0, count - 1);
+                const int pr = p_start + (t >> 5);
+                const int b = ((pr < a.ppr ? pr : pr - a.ppr) * 32 + (t & 31)) >> 2;
+                store_slot(xv[k], xrec + (b >> 2) * kRecBytes, b & 3, lane & 3, t0 < count);
             }
     }
     for (int i = tid; i < a.max_tiles * kWarps * kTileRows; i += kWarps * 32) part[i] = 0.f;
@@ -477,10 +500,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                                          : boxes_in(a.ppr - p_first) + (t_last - t_first - 1) * boxes_in(a.ppr) +
                                                boxes_in(p_end);
     const uint32_t ring_u = smem_u32(ring), xrec_u = smem_u32(xrec);
-    // Warp 4r + q takes unit slot q of boxes r, r + 4, r + 8, ...: box j sits
-    // in stage j mod 16, so every stage is read by the same four warps and
-    // each warp meets a stage's phases in order.
-    const int quad_r = warp >> 2, slot_q = warp & 3;
+    // Warp 4r + q takes unit slot q of boxes r, r + Q, r + 2Q, ... (Q quads):
+    // box j sits in stage j mod 16.  A warp never meets a stage two phases
+    // behind the box it waits for: its previous box was issued after box
+    // j - 16 (Q < 16), whose stage reuse needed box j - 32 consumed.
+    const int quad_r = warp >> 2, slot_q = warp & 3;  // quad of the warp, its unit slot in a box
     float acc0 = 0.f, acc1 = 0.f;  // rows g and g + 8 of the current row tile
     int cur = -1;
     auto flush = [&](int t) {
@@ -496,7 +520,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         acc0 = 0.f;
         acc1 = 0.f;
     };
-    for (int j = quad_r; j < nboxes && j < a.max_boxes; j += 4) {
+    for (int j = quad_r; j < nboxes && j < a.max_boxes; j += kQuads) {
         const int s = j % kStages;
         if (!mbar_wait(&full[s], (j / kStages) & 1, a.err, kErrBulkTimeout)) break;
         const uint32_t info = box_tab[j];

@@ -12,6 +12,7 @@ struct DeviceInfo {
     int sm_count = 0;
     int smem_optin = 0;     // max dynamic shared memory per block (opt-in)
     int *err = nullptr;     // device view of the mapped error word
+    bool stream_k = true;   // batched GEMMs may use the persistent stream-K schedule (KUNLUN_STREAM_K=0: never)
 };
 
 // Fused all-gather of a row-sharded batch-1 Q4_0 GEMV over peer memory
@@ -65,12 +66,16 @@ size_t q4_mma_scratch_bytes(int k, int n, int batch, const DeviceInfo &dev);
 
 // tcgen05 GEMM for batches of columns (gemm_tc.cu): rowwise-int8 with the
 // activation components already quantised (GemvRequest::q), and f16 and
-// q4_0 weights with f32 activations (which need gemm_tc_scratch_bytes of
-// scratch in GemvRequest::split).
+// q4_0 weights with f32 activations.  GemvRequest::split holds its scratch
+// (gemm_tc_scratch_bytes): the f16 activation split (f16, q4_0; required)
+// and, for shapes whose tiles would leave SMs idle, the stream-K counters
+// (which must be zero before the first launch; every launch leaves them
+// zero) and partial slots.  Without that part (e.g. the allocation-free
+// int8 entry point) every CTA computes whole tiles.
 constexpr int kTcMinBatch = 4;
 constexpr int kTcMinBatchQ4 = 4;
 bool gemm_tc_supported(int wt, int k, int n, int batch);  // (q4_0 also needs k % 64 == 0)
-size_t gemm_tc_scratch_bytes(int wt, int k, int n, int batch);
+size_t gemm_tc_scratch_bytes(int wt, int k, int n, int batch, const DeviceInfo &dev);
 cudaError_t launch_gemm_tc(const GemvRequest &r, const DeviceInfo &dev, cudaStream_t stream);
 cudaError_t launch_q4_mma_gemv(const GemvRequest &r, const DeviceInfo &dev, cudaStream_t stream);
 // One thread waits until every rank's flag in this rank's array of an

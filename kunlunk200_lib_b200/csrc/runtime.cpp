@@ -106,6 +106,8 @@ DeviceState &state(int id) {
         d.q4_mma = !(qm && std::strcmp(qm, "0") == 0);
         const char *tc = std::getenv("KUNLUN_TC");
         d.tensor_cores = !(tc && std::strcmp(tc, "0") == 0);
+        const char *sk = std::getenv("KUNLUN_STREAM_K");
+        d.info.stream_k = !(sk && std::strcmp(sk, "0") == 0);
         fail_cuda(cudaDeviceGetAttribute(&d.info.sm_count, cudaDevAttrMultiProcessorCount, id), "sm count");
         fail_cuda(cudaDeviceGetAttribute(&d.info.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, id),
                   "smem opt-in");
@@ -301,6 +303,23 @@ void grow(Kernel::Impl &s, void *&ptr, size_t &size, size_t need) {
 }
 }  // namespace
 
+namespace {
+// Scratch of the tcgen05 GEMM (activation split, stream-K counters and
+// partials) in the Kernel's split buffer; zeroed when it grows, since the
+// counters must start at zero (every launch leaves them zero).
+void tc_scratch(Kernel::Impl &s, DeviceState &d, k200::GemvRequest &r, int type, int k, int n, int batch) {
+    if (!d.tensor_cores || !k200::gemm_tc_supported(type, k, n, batch)) return;
+    const size_t need = k200::gemm_tc_scratch_bytes(type, k, n, batch, d.info);
+    if (!need) return;
+    if (s.split_size < need) {
+        grow(s, s.split, s.split_size, need);
+        fail_cuda(cudaMemsetAsync(s.split, 0, s.split_size, d.stream), "cudaMemsetAsync(split)");
+    }
+    r.split = s.split;
+    r.split_bytes = s.split_size;
+}
+}  // namespace
+
 // ---------------------------------------------------------------------------
 // matmul (src/k200.cpp:187-279)
 // ---------------------------------------------------------------------------
@@ -351,6 +370,7 @@ void matmul(Kernel &kernel, int id, void *y, const void *w, const void *x, int k
         r.q_comp = (long long)count;
         r.act_max = maxima;
         r.row_scale = scales;
+        tc_scratch(s, d, r, (int)type, k, n, batch);
     } else {
         r.x = static_cast<const float *>(x);
         const size_t need = type == WeightType::q4_0 && d.q4_mma ? k200::q4_mma_scratch_bytes(k, n, batch, d.info) : 0;
@@ -363,14 +383,7 @@ void matmul(Kernel &kernel, int id, void *y, const void *w, const void *x, int k
             r.fixup = s.fixup;
             r.fixup_bytes = s.fixup_size;
         }
-        const size_t split = d.tensor_cores && k200::gemm_tc_supported((int)type, k, n, batch)
-                                 ? k200::gemm_tc_scratch_bytes((int)type, k, n, batch)
-                                 : 0;
-        if (split) {
-            grow(s, s.split, s.split_size, split);
-            r.split = s.split;
-            r.split_bytes = s.split_size;
-        }
+        tc_scratch(s, d, r, (int)type, k, n, batch);
     }
     check((int)k200::launch_gemv(r, d.info, d.stream));
     ++d.matmuls;

@@ -91,7 +91,34 @@ def main() -> int:
                 print(f"rank {rank} step {step} gemv {i}: {len(bad)} rows differ, first {bad[:8]}", flush=True)
                 ok = False
             inp = xs[i].output(step)
+    # k200_gather_rows across the processes: an f16 batched matmul of 1025
+    # rows split 513 + 512, each slice stored into both ranks' [8][1025] outputs
+    k2, n2, batch = 1024, 1025, 8
+    torch.manual_seed(1)
+    w2 = (torch.rand(n2, k2, device="cuda") * 2 - 1).half()
+    x2 = torch.rand(batch, k2, device="cuda") * 2 - 1
+    ex2 = PeerExchange.over_group(K, dev, n2, world, rank, all_gather, batch=batch)
+    b2, c2 = row_shard(n2, world, rank)
+    mine = torch.empty(batch, c2, device="cuda")
+    K.matmul(kern, dev, mine, w2.data_ptr() + b2 * k2 * 2, x2, k2, c2, batch, K.F16)
+    dist.barrier()  # both exchanges mapped and zeroed everywhere before any rank stores
+    assert K.gather_rows(dev, ex2.view(0), b2, mine, c2, batch) == 0
+    assert K.gather_wait(dev, ex2.view(0)) == 0
+    K.select(dev)
+    status = K.wait()
+    assert status == 0, hex(status)
+    got = download(ex2.output(0), n2 * batch).reshape(batch, n2)
+    for r in range(world):
+        b, c = row_shard(n2, world, r)
+        ref = torch.empty(batch, c, device="cuda")
+        K.matmul(kern, dev, ref, w2.data_ptr() + b * k2 * 2, x2, k2, c, batch, K.F16)
+        K.select(dev)
+        K.check(K.wait())
+        if not np.array_equal(got[:, b:b + c].view(np.uint32), ref.cpu().numpy().view(np.uint32)):
+            print(f"rank {rank}: gathered slice of rank {r} differs", flush=True)
+            ok = False
     dist.barrier()  # every rank is done with the others' regions
+    ex2.close()
     for e in xs:
         e.close()
     kern.close()
