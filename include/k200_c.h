@@ -85,6 +85,13 @@ void k200_set_static_weights(int device, int enabled);
 /* Asynchronous copy on the library stream of the current device (pinned host
  * memory makes it truly asynchronous); completion via k200_wait(). */
 int k200_copy_async(void *dst, const void *src, size_t bytes, int kind);
+/* Copy by a kernel on the library stream of the current device; dst and src
+ * are device memory or pinned host memory (which the kernel accesses over
+ * the bus).  Unlike k200_copy_async, the copy takes part in the kernels'
+ * programmatic-launch chain: a matmul issued after an input copy streams its
+ * weights while the copy runs.  Completion via k200_wait(); 0 or a CUDA
+ * error code. */
+int k200_copy_kernel(void *dst, const void *src, size_t bytes);
 /* CUDA graphs of library work.  k200_graph_begin starts capturing the
  * library stream of `device`; the calls that follow on this thread that only
  * submit work (k200_copy_async, k200_matmul, k200_matmul_q4_gather, ...) are

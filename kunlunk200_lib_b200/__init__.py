@@ -61,6 +61,7 @@ _SIGNATURES = {
     "k200_stream": (C.c_void_p, [C.c_int]),
     "k200_set_stream": (None, [C.c_int, C.c_void_p]),
     "k200_set_static_weights": (None, [C.c_int, C.c_int]),
+    "k200_copy_kernel": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t]),
     "k200_graph_begin": (C.c_int, [C.c_int]),
     "k200_graph_end": (C.c_int, [C.c_int, C.POINTER(C.c_void_p)]),
     "k200_graph_launch": (C.c_int, [C.c_int, C.c_void_p]),
@@ -212,6 +213,12 @@ def copy(dst, src, nbytes: int, kind: int) -> int:
 
 def copy_async(dst, src, nbytes: int, kind: int) -> int:
     return lib().k200_copy_async(_ptr(dst), _ptr(src), nbytes, kind)
+
+
+def copy_kernel(dst, src, nbytes: int) -> int:
+    """Copy by a kernel on the current device's library stream (k200_copy_kernel);
+    either side may be pinned host memory."""
+    return lib().k200_copy_kernel(_ptr(dst), _ptr(src), nbytes)
 
 
 def peer(dst_device: int, dst, src_device: int, src, nbytes: int) -> None:

@@ -147,6 +147,13 @@ int k200_copy_async(void *dst, const void *src, size_t bytes, int kind) {
     return (int)cudaMemcpyAsync(dst, src, bytes, k, k200::library_stream(k200::current_device()));
 }
 
+int k200_copy_kernel(void *dst, const void *src, size_t bytes) {
+    std::lock_guard<std::recursive_mutex> lock(kunlun::runtime_mutex());
+    kunlun::require(k200::current_device() >= 0 && (bytes == 0 || (dst && src)));
+    const int dev = k200::current_device();
+    return (int)k200::launch_copy_kernel(dst, src, bytes, k200::device_info(dev), k200::library_stream(dev));
+}
+
 void k200_quantize_q4_0(int device, void *q4, const float *w, int k, int n) {
     std::lock_guard<std::recursive_mutex> lock(kunlun::runtime_mutex());
     kunlun::require(q4 && w && k > 0 && k % 32 == 0 && n > 0);

@@ -159,6 +159,9 @@ cudaError_t launch_common_gemv_pair(const uint8_t *w0, const uint8_t *w1, size_t
 cudaError_t launch_common_gemm_a8(const uint8_t *w, size_t scale_offset, int kp, int np, const int8_t *q,
                                   const float *row_scale, int k, int n, int m, float *y, cudaStream_t stream);
 
+// Copy by a kernel (copy.cu); either side may be pinned host memory.
+cudaError_t launch_copy_kernel(void *dst, const void *src, size_t bytes, const DeviceInfo &dev, cudaStream_t stream);
+
 // Runtime hooks (runtime.cpp).
 cudaStream_t library_stream(int device);
 const DeviceInfo &device_info(int device);

@@ -1,7 +1,8 @@
 """k200_graph_*: a decode step (host input copied in, two chained batch-1
 Q4_0 GEMVs, output copied back) recorded once through the C ABI and replayed;
 each replay must equal the same calls run directly, and must pick up new
-contents of the pinned host input buffer."""
+contents of the pinned host input buffer.  The copies are copy-engine
+transfers (k200_copy_async) or kernels (k200_copy_kernel)."""
 from __future__ import annotations
 
 import numpy as np
@@ -10,7 +11,8 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
-def test_graph_replays_decode_step(K, O, gpu):
+@pytest.mark.parametrize("kernel_copies", [False, True])
+def test_graph_replays_decode_step(K, O, gpu, kernel_copies):
     import torch
 
     k1, n1 = 1024, 2048      # up: K1 -> N1
@@ -26,10 +28,16 @@ def test_graph_replays_decode_step(K, O, gpu):
     kern = K.Kernel()
 
     def step():
-        K.check(K.copy_async(dx.data(), xh.data_ptr(), 4 * k1, K.HOST_TO_DEVICE))
+        if kernel_copies:  # k200_copy_kernel: pinned host memory read / written by a kernel
+            K.check(K.copy_kernel(dx.data(), xh.data_ptr(), 4 * k1))
+        else:
+            K.check(K.copy_async(dx.data(), xh.data_ptr(), 4 * k1, K.HOST_TO_DEVICE))
         K.matmul(kern, 0, dh, dw1, dx, k1, n1, 1, K.Q4_0)
         K.matmul(kern, 0, dy, dw2, dh, k2, n2, 1, K.Q4_0)
-        K.check(K.copy_async(yh.data_ptr(), dy.data(), 4 * n2, K.DEVICE_TO_HOST))
+        if kernel_copies:
+            K.check(K.copy_kernel(yh.data_ptr(), dy.data(), 4 * n2))
+        else:
+            K.check(K.copy_async(yh.data_ptr(), dy.data(), 4 * n2, K.DEVICE_TO_HOST))
 
     x0 = O.uniform(3, k1, -1.0, 1.0)
     xh.copy_(torch.from_numpy(x0))
