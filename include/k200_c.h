@@ -252,34 +252,43 @@ int k200_swiglu(void *kernel, int device, void *y, size_t y_bytes, const void *g
  * Replaces the gather of a row split: the reference's consumers split output
  * rows over devices and move the slices with kunlun::peer copies
  * (src/k200.cpp:89-95; "Row Split", docs/common-q4.md:23,31).  Here the GEMV
- * of each rank stores its rows straight into every rank's output buffer over
- * NVLink and then publishes a per-exchange epoch, so no separate collective
- * runs.  One process per GPU; every rank maps the other ranks' buffers with
- * k200_ipc_open.
+ * of each rank stores its rows straight into every rank's memory over NVLink,
+ * so no separate collective runs.  One process per GPU; every rank maps the
+ * other ranks' tag arrays with k200_ipc_open.
  *
- * An exchange is, on every rank, one output buffer of the full N rows, one
- * flag array of `ranks` words and two counter words, all zeroed before the
- * first call.  k200_gather describes it from this rank: y[r] and flags[r] are
- * rank r's buffer and flag array as addresses valid on this device (own
- * allocations or IPC mappings); counter is this rank's own two words.  After
- * k200_matmul_q4_gather, y[r] + row_begin .. + n on every rank holds this
- * rank's rows; once every rank's call has finished, flags on every rank hold
- * the same epoch for every rank.  wait_for (optional) names the exchange that
- * produced x: the GEMV first waits, on the device, until every rank has
- * published at least this rank's own epoch of it.  A wait that runs out
- * (several seconds) posts 0x4b03 to the device's error word
+ * An exchange is, on every rank, an output buffer y of batch * rows floats
+ * ([batch][rows]), a tag array of batch * rows 64-bit words and two counter
+ * words, all zeroed before the first call.  Values travel as tagged words
+ * {f32 bits in the low half, epoch in the high half}, each stored with one
+ * single-copy-atomic 8-byte store into every rank's tag array; the epoch
+ * counts this rank's launches on the exchange (the counter's second word).
+ * A reader therefore needs no flag: it waits on the device until each word
+ * it reads carries its own rank's current epoch.  k200_gather describes an
+ * exchange from this rank: tags[r] is rank r's tag array as an address valid
+ * on this device (own allocation or IPC mapping); y and counter are this
+ * rank's own.  k200_matmul_q4_gather (batch 1) stores this rank's rows
+ * [row_begin, row_begin + n) as tagged words on every rank and as plain
+ * floats into this rank's y; k200_gather_wait then waits for every word of
+ * the exchange and writes all batch * rows values into this rank's y.
+ * wait_for (optional) names the exchange whose output is x (x must point
+ * into wait_for's y): the GEMV reads x's tagged words, each as it arrives,
+ * and x's elements past batch * rows (padding) plainly from y.  A wait that
+ * runs out (several seconds) posts 0x4b03 to the device's error word
  * (k200_wait returns it) and the call completes without waiting further.
  * Calls on one exchange must be issued in the same order on every rank, on
- * one stream per rank.  A rank that reuses an output buffer while another
- * rank may still read the previous contents races: alternate two buffers. */
+ * one stream per rank.  A rank that reuses an exchange while another rank
+ * may still read the previous contents races: alternate two exchanges (a
+ * rank cannot run further ahead than one use, because its next reader waits
+ * for every rank's words). */
 #define K200_GATHER_MAX_RANKS 8
 #define K200_GATHER_UNSUPPORTED (-4)
 typedef struct {
     int ranks, rank;
-    float *y[K200_GATHER_MAX_RANKS];
-    unsigned *flags[K200_GATHER_MAX_RANKS];
-    unsigned *counter;
-    int rows; /* rows of every rank's output buffer: row_begin + n must not exceed it */
+    unsigned long long *tags[K200_GATHER_MAX_RANKS]; /* every rank's tag array */
+    float *y;                                          /* this rank's output buffer */
+    unsigned *counter;                                 /* this rank's two counter words */
+    int rows;  /* rows of every rank's buffers: row_begin + n must not exceed it */
+    int batch; /* columns: [batch][rows] values (1 for k200_matmul_q4_gather) */
 } k200_gather;
 /* IPC of a device allocation's base address (64-byte handles). */
 int k200_ipc_handle(const void *device_ptr, void *handle);
@@ -292,18 +301,20 @@ size_t k200_matmul_q4_gather_scratch(int device, int k, int n);
  * above, left zeroed.  0, K200_GATHER_UNSUPPORTED or a CUDA error code. */
 int k200_matmul_q4_gather(int device, const k200_gather *out, int row_begin, const void *w, const void *x, int k,
                           int n, void *scratch, size_t scratch_bytes, const k200_gather *wait_for);
-/* The wait alone (for the last exchange of a sequence). */
+/* Waits for every tagged word of an exchange to carry this rank's current
+ * epoch and writes the values into this rank's y (the end of a sequence, or
+ * before the host reads y). */
 int k200_gather_wait(int device, const k200_gather *exchange);
 /* Row gather for any row-sharded matmul (any weight type and batch, any
  * split of the rows, uneven ones included): this rank's slice, [batch][n]
  * floats at `shard` (device memory, e.g. the y of a k200_matmul over this
- * rank's n weight rows), is stored into columns [row_begin, row_begin + n) of
- * every rank's [batch][rows] output buffer, then the exchange's epoch is
- * published as k200_matmul_q4_gather does; readers wait with
- * k200_gather_wait (or wait_for).  Each buffer y[r] must hold batch * rows
- * floats.  Asynchronous on the library stream; 0 or a CUDA error code.
- * Replaces the reference consumers' per-slice kunlun::peer copies of a row
- * split (src/k200.cpp:89-95, docs/common-q4.md "Row Split"). */
+ * rank's n weight rows), is stored as tagged words into columns
+ * [row_begin, row_begin + n) of every rank's [batch][rows] tag array and as
+ * plain floats into this rank's y; readers wait with k200_gather_wait (or
+ * wait_for).  batch must equal the exchange's batch.  Asynchronous on the
+ * library stream; 0 or a CUDA error code.  Replaces the reference
+ * consumers' per-slice kunlun::peer copies of a row split
+ * (src/k200.cpp:89-95, docs/common-q4.md "Row Split"). */
 int k200_gather_rows(int device, const k200_gather *out, int row_begin, const float *shard, int n, int batch);
 
 #ifdef __cplusplus

@@ -773,10 +773,11 @@ IPC_HANDLE_BYTES = 64
 
 
 class GatherView(C.Structure):
-    """k200_gather: one exchange seen from one rank (addresses valid on its device)."""
-    _fields_ = [("ranks", C.c_int), ("rank", C.c_int), ("y", C.c_void_p * GATHER_MAX_RANKS),
-                ("flags", C.c_void_p * GATHER_MAX_RANKS), ("counter", C.c_void_p),
-                ("rows", C.c_int)]
+    """k200_gather: one exchange seen from one rank (addresses valid on its device): every
+    rank's tag array of [batch][rows] 64-bit words {f32, epoch}, this rank's [batch][rows]
+    output buffer and this rank's two counter words."""
+    _fields_ = [("ranks", C.c_int), ("rank", C.c_int), ("tags", C.c_void_p * GATHER_MAX_RANKS),
+                ("y", C.c_void_p), ("counter", C.c_void_p), ("rows", C.c_int), ("batch", C.c_int)]
 
 
 def ipc_handle(ptr) -> bytes:
@@ -804,7 +805,9 @@ def matmul_q4_gather_scratch(device: int, k: int, n: int) -> int:
 
 def matmul_q4_gather(device: int, out: GatherView, row_begin: int, w, x, k: int, n: int, scratch,
                      scratch_bytes: int, wait_for: GatherView | None = None) -> int:
-    """This rank's rows of Y = W.x stored into every rank's output (k200_matmul_q4_gather).
+    """This rank's rows of Y = W.x stored as tagged words into every rank's tag array and as
+    plain floats into this rank's y (k200_matmul_q4_gather); with wait_for, x points into that
+    exchange's y and is read from its tagged words as they arrive.
 
     Returns 0, GATHER_UNSUPPORTED or a CUDA error code; asynchronous on the library stream.
     """
@@ -813,12 +816,14 @@ def matmul_q4_gather(device: int, out: GatherView, row_begin: int, w, x, k: int,
 
 
 def gather_rows(device: int, out: GatherView, row_begin: int, shard, n: int, batch: int = 1) -> int:
-    """This rank's [batch][n] slice into columns row_begin.. of every rank's [batch][rows] output
-    (k200_gather_rows); 0 or a CUDA error code, asynchronous on the library stream."""
+    """This rank's [batch][n] slice into columns row_begin.. of every rank's [batch][rows] tag
+    array and of this rank's y (k200_gather_rows); 0 or a CUDA error code, asynchronous on the
+    library stream."""
     return lib().k200_gather_rows(device, C.addressof(out), row_begin, _ptr(shard), n, batch)
 
 
 def gather_wait(device: int, exchange: GatherView) -> int:
-    """Device-side wait until every rank has published this rank's epoch of `exchange`."""
+    """Device-side wait until every tagged word of `exchange` carries this rank's epoch, then
+    the values written into this rank's y (k200_gather_wait)."""
     return lib().k200_gather_wait(device, C.addressof(exchange))
 

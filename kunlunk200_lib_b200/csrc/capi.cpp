@@ -5,6 +5,7 @@
 
 #include <cuda_runtime.h>
 
+#include <climits>
 #include <cstring>
 
 #include "k200_internal.h"
@@ -17,20 +18,20 @@ size_t matmul_count(int device);
 bool common_q4_pack(const void *raw, size_t bytes, int k, int n, void *out, size_t out_bytes);
 size_t peer_copy_count();
 size_t peer_byte_count();
-int matmul_q4_gather(int device, const GatherLaunch &g, const void *w, const void *x, int k, int n, void *scratch,
-                     size_t scratch_bytes);
-int gather_wait(int device, const unsigned *flags, int ranks, int rank);
-int gather_rows(int device, const GatherLaunch &g, const float *shard, int n, int batch, int rows);
+int matmul_q4_gather(int device, const GatherLaunch &g, float *y, const void *w, const void *x, int k, int n,
+                     void *scratch, size_t scratch_bytes);
+int gather_wait(int device, const unsigned long long *tags, float *y, long long count, const unsigned *counter);
+int gather_rows(int device, const GatherLaunch &g, float *y, const float *shard, int n, int batch, int rows);
 size_t q4_gather_scratch(int device, int k, int n);
 }  // namespace k200
 
 namespace {
 bool gather_ok(const k200_gather *g) {
     if (!g || g->ranks < 1 || g->ranks > K200_GATHER_MAX_RANKS || g->rank < 0 || g->rank >= g->ranks || !g->counter ||
-        g->rows < 1)
+        !g->y || g->rows < 1 || g->batch < 1 || (long long)g->rows * g->batch > INT_MAX)
         return false;
     for (int r = 0; r < g->ranks; ++r)
-        if (!g->y[r] || !g->flags[r]) return false;
+        if (!g->tags[r]) return false;
     return true;
 }
 }  // namespace
@@ -225,42 +226,43 @@ size_t k200_matmul_q4_gather_scratch(int device, int k, int n) { return k200::q4
 int k200_matmul_q4_gather(int device, const k200_gather *out, int row_begin, const void *w, const void *x, int k,
                           int n, void *scratch, size_t scratch_bytes, const k200_gather *wait_for) {
     static_assert(K200_GATHER_MAX_RANKS == k200::kGatherMaxRanks, "k200_c.h rank limit out of date");
-    kunlun::require(gather_ok(out) && (!wait_for || gather_ok(wait_for)) && row_begin >= 0 && n > 0);
-    // the rows are stored into every rank's buffer, over NVLink for the others
-    kunlun::require(n <= out->rows && row_begin <= out->rows - n);
+    kunlun::require(gather_ok(out) && (!wait_for || gather_ok(wait_for)) && row_begin >= 0 && n > 0 && x);
+    // one column: the rows are stored as tagged words into every rank's tag array
+    kunlun::require(out->batch == 1 && n <= out->rows && row_begin <= out->rows - n);
     k200::GatherLaunch g;
     g.ranks = out->ranks;
     g.rank = out->rank;
-    for (int r = 0; r < out->ranks; ++r) {
-        g.y[r] = out->y[r] + row_begin;
-        g.flags[r] = out->flags[r];
-    }
+    for (int r = 0; r < out->ranks; ++r) g.tags[r] = out->tags[r] + row_begin;
     g.counter = out->counter;
     if (wait_for) {
-        g.wait_flags = wait_for->flags[wait_for->rank];
-        g.wait_ranks = wait_for->ranks;
-        g.wait_rank = wait_for->rank;
+        // X lies in wait_for's own output buffer; its tagged words sit at the same offset
+        const float *base = wait_for->y;
+        const float *xf = static_cast<const float *>(x);
+        const long long extent = (long long)wait_for->rows * wait_for->batch;
+        kunlun::require(xf >= base && xf - base <= extent);
+        const long long offset = xf - base;
+        g.wait_tags = wait_for->tags[wait_for->rank] + offset;
+        g.wait_counter = wait_for->counter;
+        g.wait_tagged = (int)(extent - offset);
     }
-    return k200::matmul_q4_gather(device, g, w, x, k, n, scratch, scratch_bytes);
+    return k200::matmul_q4_gather(device, g, out->y + row_begin, w, x, k, n, scratch, scratch_bytes);
 }
 
 int k200_gather_rows(int device, const k200_gather *out, int row_begin, const float *shard, int n, int batch) {
     kunlun::require(gather_ok(out) && shard && row_begin >= 0 && n > 0 && batch > 0);
-    kunlun::require(n <= out->rows && row_begin <= out->rows - n);
+    kunlun::require(batch == out->batch && n <= out->rows && row_begin <= out->rows - n);
     k200::GatherLaunch g;
     g.ranks = out->ranks;
     g.rank = out->rank;
-    for (int r = 0; r < out->ranks; ++r) {
-        g.y[r] = out->y[r] + row_begin;
-        g.flags[r] = out->flags[r];
-    }
+    for (int r = 0; r < out->ranks; ++r) g.tags[r] = out->tags[r] + row_begin;
     g.counter = out->counter;
-    return k200::gather_rows(device, g, shard, n, batch, out->rows);
+    return k200::gather_rows(device, g, out->y + row_begin, shard, n, batch, out->rows);
 }
 
 int k200_gather_wait(int device, const k200_gather *exchange) {
     kunlun::require(gather_ok(exchange));
-    return k200::gather_wait(device, exchange->flags[exchange->rank], exchange->ranks, exchange->rank);
+    return k200::gather_wait(device, exchange->tags[exchange->rank], exchange->y,
+                             (long long)exchange->rows * exchange->batch, exchange->counter);
 }
 
 // ---- native Q4 layout ---------------------------------------------------------

@@ -60,7 +60,7 @@
 
 #include "device_common.cuh"
 #include "k200_internal.h"
-#include "peer_flags.cuh"
+#include "exchange.cuh"
 
 namespace k200 {
 
@@ -248,18 +248,58 @@ __device__ __forceinline__ int cta_of(uint32_t u, uint32_t units, int grid) {
 // x[a1+1] and the same +16 (see lane_bytes); store_slot scales the block by
 // 2^-e so that its largest magnitude lies in [2^14, 2^15), splits the values
 // into f16 hi + lo and stores them (all 32 lanes of the warp must call it).
-// (peer: X was written by other GPUs during this launch's lifetime; read it
-// through L2 rather than the read-only path)
-__device__ __forceinline__ void load_slot(const float *xb, int p, int c, float (&v)[8], bool peer) {
+__device__ __forceinline__ void load_slot(const float *xb, int p, int c, float (&v)[8]) {
     const int a0 = pair_first(p, c), a1 = pair_second(p, c);
     const float2 *q0 = reinterpret_cast<const float2 *>(xb + a0), *q1 = reinterpret_cast<const float2 *>(xb + a1);
-    const float2 l0 = peer ? __ldcg(q0) : __ldg(q0);
-    const float2 l1 = peer ? __ldcg(q1) : __ldg(q1);
-    const float2 h0 = peer ? __ldcg(q0 + 8) : __ldg(q0 + 8);
-    const float2 h1 = peer ? __ldcg(q1 + 8) : __ldg(q1 + 8);
+    const float2 l0 = __ldg(q0);
+    const float2 l1 = __ldg(q1);
+    const float2 h0 = __ldg(q0 + 8);
+    const float2 h1 = __ldg(q1 + 8);
     // register order = fragment order: {q0, q2}, {q0+16, q2+16}, {q1, q3}, {q1+16, q3+16}
     v[0] = l0.x; v[1] = l1.x; v[2] = h0.x; v[3] = h1.x;
     v[4] = l0.y; v[5] = l1.y; v[6] = h0.y; v[7] = h1.y;
+}
+
+// The same eight activations when X is another exchange's output: tagged
+// words {f32, epoch} (exchange.cuh) for the block's first `lim` elements,
+// plain floats after them (the zeroed padding past the exchange's rows).
+// issue_slot_tagged starts the 16-byte loads of the tagged element pairs;
+// resolve_slot_tagged waits for words that do not carry `epoch` yet and
+// returns the values in load_slot's order.
+__device__ __forceinline__ void issue_slot_tagged(const unsigned long long *tb, int lim, int p, int c,
+                                                  unsigned long long (&w)[8]) {
+    const int a0 = pair_first(p, c), a1 = pair_second(p, c);
+    const int e[4] = {a0, a1, a0 + 16, a1 + 16};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        if (e[q] + 1 < lim) {
+            ld_tag2(tb + e[q], w[2 * q], w[2 * q + 1]);
+        } else {
+            w[2 * q] = 0ull;
+            w[2 * q + 1] = 0ull;
+        }
+    }
+}
+__device__ __forceinline__ void resolve_slot_tagged(const unsigned long long *tb, const float *xb, int lim, int p,
+                                                    int c, const unsigned long long (&w)[8], unsigned epoch,
+                                                    int *err, float (&v)[8]) {
+    const int a0 = pair_first(p, c), a1 = pair_second(p, c);
+    const int e[4] = {a0, a1, a0 + 16, a1 + 16};
+    float2 f[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        if (e[q] + 1 < lim) {
+            f[q].x = await_tag(tb + e[q], w[2 * q], epoch, err);
+            f[q].y = await_tag(tb + e[q] + 1, w[2 * q + 1], epoch, err);
+        } else if (e[q] >= lim) {
+            f[q] = __ldcg(reinterpret_cast<const float2 *>(xb + e[q]));
+        } else {  // the last tagged element, then padding
+            f[q].x = await_tag(tb + e[q], ld_tag(tb + e[q]), epoch, err);
+            f[q].y = __ldcg(xb + e[q] + 1);
+        }
+    }
+    v[0] = f[0].x; v[1] = f[1].x; v[2] = f[2].x; v[3] = f[3].x;
+    v[4] = f[0].y; v[5] = f[1].y; v[6] = f[2].y; v[7] = f[3].y;
 }
 
 __device__ __forceinline__ void store_slot(const float (&v)[8], uint8_t *rec, int p, int c, bool store) {
@@ -319,7 +359,7 @@ constexpr uint32_t kPeerBudget = 1u << 20;   // polls of a partial sum (with 64 
 // the plain GEMV carries none of its code or registers.
 template <bool kGather>
 __global__ void __launch_bounds__(kThreads, 1)
-    q4_mma_gemv_kernel(const __grid_constant__ Q4MmaMaps maps, const Q4MmaArgs a, const GatherLaunch xg) {
+    q4_mma_gemv_kernel(const __grid_constant__ Q4MmaMaps maps, const Q4MmaArgs a, const __grid_constant__ GatherLaunch xg) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int groups = a.k >> 7;
     uint8_t *ring = smem;
@@ -376,13 +416,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 
     // ---------------- consumers ----------------
-    pdl_wait_prior();  // x, y and the partial-sum words may belong to the previous kernel
-    const bool peer_x = kGather && xg.wait_flags != nullptr;
-    if (peer_x) {
-        // X is the output of another exchange: every rank must have stored its rows
-        if (tid == 0) wait_peer_flags(xg.wait_flags, xg.wait_ranks, xg.wait_rank, a.err);
-        consumer_sync();
-    }
+    pdl_wait_prior();  // x, y, the partial-sum words and the exchange counters may belong to earlier kernels
+    // X from another exchange (its tagged words, as every rank's rows arrive)
+    const bool peer_x = kGather && xg.wait_tags != nullptr;
+    const unsigned wait_epoch = peer_x ? exchange_epoch(xg.wait_counter) : 0u;
+    // this launch's epoch of its own exchange
+    const unsigned epoch = kGather && xg.ranks > 0 ? exchange_epoch(xg.counter) + 1u : 0u;
     {
         // fragment records: four threads per activation block; every load of a
         // thread is issued before the first conversion.  Only the unit pairs
@@ -402,14 +441,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const int count = 32 * npairs;  // a multiple of 32: whole warps are inside or past the range
         float xv[kPasses][8];
+        if (kGather && peer_x) {
+            // tagged words: every load of the thread is issued before the first wait
+            unsigned long long xw[kPasses][8];
 #pragma unroll
-        for (int k = 0; k < kPasses; ++k)
-            if (k * kWarps * 32 < count) {
-                const int t = min(k * kWarps * 32 + tid, count - 1);
-                const int pr = p_start + (t >> 5);
-                const int b = ((pr < a.ppr ? pr : pr - a.ppr) * 32 + (t & 31)) >> 2;
-                load_slot(a.x + 32 * b, b & 3, lane & 3, xv[k], peer_x);
-            }
+            for (int k = 0; k < kPasses; ++k)
+                if (k * kWarps * 32 < count) {
+                    const int t = min(k * kWarps * 32 + tid, count - 1);
+                    const int pr = p_start + (t >> 5);
+                    const int b = ((pr < a.ppr ? pr : pr - a.ppr) * 32 + (t & 31)) >> 2;
+                    issue_slot_tagged(xg.wait_tags + 32 * b, xg.wait_tagged - 32 * b, b & 3, lane & 3, xw[k]);
+                }
+#pragma unroll
+            for (int k = 0; k < kPasses; ++k)
+                if (k * kWarps * 32 < count) {
+                    const int t = min(k * kWarps * 32 + tid, count - 1);
+                    const int pr = p_start + (t >> 5);
+                    const int b = ((pr < a.ppr ? pr : pr - a.ppr) * 32 + (t & 31)) >> 2;
+                    resolve_slot_tagged(xg.wait_tags + 32 * b, a.x + 32 * b, xg.wait_tagged - 32 * b, b & 3,
+                                        lane & 3, xw[k], wait_epoch, a.err, xv[k]);
+                }
+        } else {
+#pragma unroll
+            for (int k = 0; k < kPasses; ++k)
+                if (k * kWarps * 32 < count) {
+                    const int t = min(k * kWarps * 32 + tid, count - 1);
+                    const int pr = p_start + (t >> 5);
+                    const int b = ((pr < a.ppr ? pr : pr - a.ppr) * 32 + (t & 31)) >> 2;
+                    load_slot(a.x + 32 * b, b & 3, lane & 3, xv[k]);
+                }
+        }
 #pragma unroll
         for (int k = 0; k < kPasses; ++k)
             if (k * kWarps * 32 < count) {
@@ -486,10 +547,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (row < a.n) {
             a.y[row] = v;
-            // fused all-gather: the same row into every other rank's output
-            if (kGather)
-                for (int r = 0; r < xg.ranks; ++r)
-                    if (r != xg.rank) xg.y[r][row] = v;
+            // fused all-gather: the row as a tagged word into every rank's tag array
+            if (kGather) {
+                const unsigned long long w = tag_word(v, epoch);
+                for (int r = 0; r < xg.ranks; ++r) st_tag(xg.tags[r] + row, w);
+            }
         }
     };
 
@@ -581,20 +643,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     consumer_sync();  // every warp's partials are in shared memory
     for (int ts = warp; ts <= t_last - t_first; ts += kWarps) finish_tile(ts);
     if (kGather && xg.ranks > 0) {
-        // The last block of the launch to get here publishes the exchange's
-        // next epoch on every rank, after every block's row stores: the
-        // barrier orders this block's stores before thread 0's system-scope
-        // fence, which orders them before its arrival (one fence per block;
-        // a fence in every thread costs microseconds each).
+        // every consumer thread has read the epoch: count the block in (the
+        // last one raises the exchange's epoch for the launches that follow)
         consumer_sync();
-        if (tid == 0) publish_epoch(xg, a.grid);
+        if (tid == 0) count_launch(xg.counter, a.grid, epoch);
     }
 }
 
-// Waits, in one thread, for an exchange's flags (launch_gather_wait).
-__global__ void gather_wait_kernel(const unsigned *flags, int ranks, int rank, int *err) {
-    pdl_wait_prior();
-    if (threadIdx.x == 0) wait_peer_flags(flags, ranks, rank, err);
+// The end of a sharded sequence (launch_gather_wait): waits for the first
+// `count` words of this rank's tag array of an exchange to carry this rank's
+// current epoch of it, and stores their values as the exchange's plain rows.
+__global__ void __launch_bounds__(256) gather_wait_kernel(const unsigned long long *tags, float *y, long long count,
+                                                          const unsigned *counter, int *err) {
+    pdl_wait_prior();  // the counter belongs to the kernels that stored into the exchange
+    const unsigned epoch = exchange_epoch(counter);
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < count;
+         i += static_cast<long long>(gridDim.x) * blockDim.x)
+        y[i] = await_tag(tags + i, ld_tag(tags + i), epoch, err);
 }
 
 struct Q4MmaPlan {
@@ -733,18 +798,20 @@ cudaError_t launch_q4_mma_gemv(const GemvRequest &r, const DeviceInfo &dev, cuda
     return cudaLaunchKernelEx(&cfg, kernel, maps, a, xg);
 }
 
-cudaError_t launch_gather_wait(const unsigned *flags, int ranks, int rank, const DeviceInfo &dev,
-                               cudaStream_t stream) {
+cudaError_t launch_gather_wait(const unsigned long long *tags, float *y, long long count, const unsigned *counter,
+                               const DeviceInfo &dev, cudaStream_t stream) {
+    if (!tags || !y || !counter || count < 1) return cudaErrorInvalidValue;
+    const long long want = (count + 255) / 256;
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(1);
-    cfg.blockDim = dim3(32);
+    cfg.gridDim = dim3(static_cast<unsigned>(want < dev.sm_count * 2LL ? want : dev.sm_count * 2LL));
+    cfg.blockDim = dim3(256);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gather_wait_kernel, flags, ranks, rank, dev.err);
+    return cudaLaunchKernelEx(&cfg, gather_wait_kernel, tags, y, count, counter, dev.err);
 }
 
 }  // namespace k200

@@ -15,21 +15,20 @@ struct DeviceInfo {
     bool stream_k = true;   // batched GEMMs may use the persistent stream-K schedule (KUNLUN_STREAM_K=0: never)
 };
 
-// Fused all-gather of a row-sharded batch-1 Q4_0 GEMV over peer memory
-// (k200_matmul_q4_gather): the rows this rank computes are stored into every
-// rank's output buffer, and the last block of the launch then publishes the
-// exchange's new epoch in every rank's flag array.  A launch can first wait
-// until every rank has published at least this rank's own epoch of another
-// exchange (the one that produced its X).
+// Fused all-gather of a row-sharded matmul over peer memory (k200_gather,
+// exchange.cuh): the values this rank computes are stored as tagged words
+// {f32, epoch} into every rank's tag array of the exchange, and the launch's
+// last block raises this rank's epoch of it.  A batch-1 Q4_0 GEMV can read
+// its X from another exchange's tags, waiting for each word's epoch.
 constexpr int kGatherMaxRanks = 8;
 constexpr int kGatherUnsupported = -4;  // K200_GATHER_UNSUPPORTED
 struct GatherLaunch {
-    int ranks = 0, rank = 0;                    // ranks 0: no gather
-    float *y[kGatherMaxRanks] = {};             // every rank's output rows (offset to this shard)
-    unsigned *flags[kGatherMaxRanks] = {};      // every rank's flag array of the exchange
-    unsigned *counter = nullptr;                // this rank's {arrivals, epoch} words
-    const unsigned *wait_flags = nullptr;       // this rank's flag array of the exchange that made X
-    int wait_ranks = 0, wait_rank = 0;
+    int ranks = 0, rank = 0;                          // ranks 0: no gather
+    unsigned long long *tags[kGatherMaxRanks] = {};   // every rank's tag array (offset to this shard)
+    unsigned *counter = nullptr;                      // this rank's {arrivals, epoch} words
+    const unsigned long long *wait_tags = nullptr;    // this rank's tags of the exchange that made X, at X[0]
+    const unsigned *wait_counter = nullptr;           // this rank's counter of that exchange
+    int wait_tagged = 0;                              // X[0, wait_tagged) is tagged; the rest is read plain
 };
 
 // One legacy matmul launch: Y[c, r] = W[r, :] . X[c, :].
@@ -78,14 +77,16 @@ bool gemm_tc_supported(int wt, int k, int n, int batch);  // (q4_0 also needs k 
 size_t gemm_tc_scratch_bytes(int wt, int k, int n, int batch, const DeviceInfo &dev);
 cudaError_t launch_gemm_tc(const GemvRequest &r, const DeviceInfo &dev, cudaStream_t stream);
 cudaError_t launch_q4_mma_gemv(const GemvRequest &r, const DeviceInfo &dev, cudaStream_t stream);
-// One thread waits until every rank's flag in this rank's array of an
-// exchange has reached this rank's own (kErrPeerTimeout after its budget).
-cudaError_t launch_gather_wait(const unsigned *flags, int ranks, int rank, const DeviceInfo &dev,
-                               cudaStream_t stream);
-// Row gather (gather.cu): [batch][n] slice -> columns of every rank's
-// [batch][rows] output (xg.y[r] point at the slice's first column), then the
-// exchange's next epoch.
-cudaError_t launch_gather_rows(const GatherLaunch &xg, const float *shard, int n, int batch, int rows,
+// Waits for the first `count` tagged words of this rank's tag array of an
+// exchange to carry this rank's current epoch and stores their values into
+// y (kErrPeerTimeout after the budget).
+cudaError_t launch_gather_wait(const unsigned long long *tags, float *y, long long count, const unsigned *counter,
+                               const DeviceInfo &dev, cudaStream_t stream);
+// Row gather (gather.cu): [batch][n] slice -> tagged words in columns of
+// every rank's [batch][rows] tag array (xg.tags[r] point at the slice's
+// first column) and plain values in this rank's own [batch][rows] output y
+// (at the slice's first column), then the exchange's next epoch.
+cudaError_t launch_gather_rows(const GatherLaunch &xg, float *y, const float *shard, int n, int batch, int rows,
                                const DeviceInfo &dev, cudaStream_t stream);
 // Row gathers (get_rows.cu); an index outside [0, n) writes no output and
 // sets *status to 1 (else 0).

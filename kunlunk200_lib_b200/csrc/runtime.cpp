@@ -618,15 +618,14 @@ size_t q4_gather_scratch(int id, int k, int n) {
 // Batch-1 Q4_0 GEMV of this rank's rows with the fused all-gather
 // (k200_matmul_q4_gather).  Only the tensor-core GEMV stores rows to peers,
 // so a shape it does not take is declined, never run another way.
-int matmul_q4_gather(int id, const GatherLaunch &g, const void *w, const void *x, int k, int n, void *scratch,
-                     size_t scratch_bytes) {
+int matmul_q4_gather(int id, const GatherLaunch &g, float *y, const void *w, const void *x, int k, int n,
+                     void *scratch, size_t scratch_bytes) {
     using namespace kunlun;
     std::lock_guard<std::recursive_mutex> lock(mutex);
     require(id >= 0 && id < cuda_device_count());
-    require(k > 0 && k <= 16384 && k % 32 == 0 && n > 0 && w && x && scratch);
+    require(k > 0 && k <= 16384 && k % 32 == 0 && n > 0 && w && x && y && scratch);
     require(g.ranks >= 1 && g.ranks <= kGatherMaxRanks && g.rank >= 0 && g.rank < g.ranks && g.counter);
-    require(!g.wait_flags || (g.wait_ranks >= 1 && g.wait_ranks <= kGatherMaxRanks && g.wait_rank >= 0 &&
-                              g.wait_rank < g.wait_ranks));
+    require(!g.wait_tags || (g.wait_counter && g.wait_tagged >= 0));
     select(id);
     DeviceState &d = state(id);
     const size_t need = q4_mma_scratch_bytes(k, n, 1, d.info);
@@ -636,7 +635,7 @@ int matmul_q4_gather(int id, const GatherLaunch &g, const void *w, const void *x
     r.wt = (int)WeightType::q4_0;
     r.w = w;
     r.x = static_cast<const float *>(x);
-    r.y = g.y[g.rank];
+    r.y = y;
     r.k = k;
     r.n = n;
     r.batch = 1;
@@ -653,25 +652,24 @@ int matmul_q4_gather(int id, const GatherLaunch &g, const void *w, const void *x
     return 0;
 }
 
-int gather_rows(int id, const GatherLaunch &g, const float *shard, int n, int batch, int rows) {
+int gather_rows(int id, const GatherLaunch &g, float *y, const float *shard, int n, int batch, int rows) {
     using namespace kunlun;
     std::lock_guard<std::recursive_mutex> lock(mutex);
-    require(id >= 0 && id < cuda_device_count() && shard && n > 0 && batch > 0 && rows >= n);
+    require(id >= 0 && id < cuda_device_count() && y && shard && n > 0 && batch > 0 && rows >= n);
     require(g.ranks >= 1 && g.ranks <= kGatherMaxRanks && g.rank >= 0 && g.rank < g.ranks && g.counter);
     require((size_t)batch * (size_t)rows <= (size_t)INT_MAX);
     select(id);
     DeviceState &d = state(id);
-    return (int)launch_gather_rows(g, shard, n, batch, rows, d.info, d.stream);
+    return (int)launch_gather_rows(g, y, shard, n, batch, rows, d.info, d.stream);
 }
 
-int gather_wait(int id, const unsigned *flags, int ranks, int rank) {
+int gather_wait(int id, const unsigned long long *tags, float *y, long long count, const unsigned *counter) {
     using namespace kunlun;
     std::lock_guard<std::recursive_mutex> lock(mutex);
-    require(id >= 0 && id < cuda_device_count() && flags && ranks >= 1 && ranks <= kGatherMaxRanks && rank >= 0 &&
-            rank < ranks);
+    require(id >= 0 && id < cuda_device_count() && tags && y && counter && count >= 1);
     select(id);
     DeviceState &d = state(id);
-    return (int)launch_gather_wait(flags, ranks, rank, d.info, d.stream);
+    return (int)launch_gather_wait(tags, y, count, counter, d.info, d.stream);
 }
 
 // Rowwise-int8 matmul whose activation scratch is the module's static array

@@ -58,15 +58,16 @@ class PeerExchange:
     (k200_matmul_q4_gather for the batch-1 Q4_0 GEMV, k200_gather_rows for any
     matmul).
 
-    Every rank owns one device region, zeroed at creation:
-      ``buffers`` output buffers of [batch][n] floats (each padded to a
-      multiple of 64 floats), then the exchange's flag array (``world``
-      words, padded to 64 bytes), then this rank's two counter words.
-    ``bases[r]`` is rank r's region as an address valid on this rank's device
-    (its own allocation, or an IPC mapping of the other rank's).  ``view(b)``
-    is the k200_gather of output buffer b; alternate buffers between
-    consecutive uses, so that a rank that runs ahead never overwrites rows
-    another rank is still reading.
+    Every rank owns one device region, zeroed at creation, holding
+    ``buffers`` exchanges: their output buffers of [batch][n] floats (each
+    padded to a multiple of 64 values), then their tag arrays of as many
+    64-bit words {f32, epoch}, then their counters (two words each, 64 bytes
+    apart).  ``bases[r]`` is rank r's region as an address valid on this
+    rank's device (its own allocation, or an IPC mapping of the other
+    rank's); other ranks only ever store into the tag arrays.  ``view(b)`` is
+    the k200_gather of exchange b; alternate exchanges between consecutive
+    uses, so that a rank that runs ahead never overwrites words another rank
+    is still reading.
     """
 
     def __init__(self, K, device: int, n: int, world: int, rank: int, bases: list[int], buffers: int = 2,
@@ -77,16 +78,17 @@ class PeerExchange:
         self.batch = batch
         self.n_pad = self.padded(n * batch)
         self._owned, self._mapped = owned, list(mapped)
-        flags_off = buffers * self.n_pad * 4
+        tags_off = buffers * self.n_pad * 4
+        counters_off = tags_off + buffers * self.n_pad * 8
         self.views = []
         for b in range(buffers):
             v = K.GatherView()
             v.ranks, v.rank = world, rank
             for r in range(world):
-                v.y[r] = bases[r] + b * self.n_pad * 4
-                v.flags[r] = bases[r] + flags_off
-            v.counter = bases[rank] + flags_off + 64
-            v.rows = n
+                v.tags[r] = bases[r] + tags_off + b * self.n_pad * 8
+            v.y = bases[rank] + b * self.n_pad * 4
+            v.counter = bases[rank] + counters_off + b * 64
+            v.rows, v.batch = n, batch
             self.views.append(v)
 
     @staticmethod
@@ -95,7 +97,7 @@ class PeerExchange:
 
     @classmethod
     def region_bytes(cls, n: int, buffers: int = 2, batch: int = 1) -> int:
-        return buffers * cls.padded(n * batch) * 4 + 128
+        return buffers * (cls.padded(n * batch) * 12 + 64)
 
     @classmethod
     def _region(cls, K, device: int, n: int, buffers: int, batch: int = 1):
@@ -135,8 +137,9 @@ class PeerExchange:
         return self.views[b % self.buffers]
 
     def output(self, b: int) -> int:
-        """Address of this rank's own output buffer b (the full [batch][n] rows)."""
-        return self.views[b % self.buffers].y[self.rank]
+        """Address of this rank's own output buffer b (the full [batch][n] rows once
+        k200_gather_wait has run on it; this rank's own rows as soon as they are computed)."""
+        return self.views[b % self.buffers].y
 
     def close(self) -> None:
         for p in self._mapped:

@@ -78,6 +78,9 @@ def main() -> int:
                                     scratch.data_ptr(), nbytes, wait_for=None if i == 0 else xs[0].view(step))
             assert rc == 0, rc
             inp = xs[i].output(step)
+        # the values of both exchanges as plain rows (the down GEMV read the up
+        # exchange's tagged words directly)
+        assert K.gather_wait(dev, xs[0].view(step)) == 0
         assert K.gather_wait(dev, xs[1].view(step)) == 0
         K.select(dev)
         status = K.wait()

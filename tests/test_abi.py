@@ -141,8 +141,8 @@ def test_reference_consumers_link_against_this_library():
 
 # a well-formed two-rank exchange view (dummy addresses) that each case then breaks
 _GATHER = ("v = K.GatherView()\nv.ranks, v.rank = 2, 0\n"
-           "for r in range(2):\n    v.y[r] = 4096 * (r + 1)\n    v.flags[r] = 65536 * (r + 1)\n"
-           "v.counter = 1 << 20\nv.rows = 64\n")
+           "for r in range(2):\n    v.tags[r] = 65536 * (r + 1)\n"
+           "v.y = 4096\nv.counter = 1 << 20\nv.rows, v.batch = 64, 1\n")
 
 
 def _run_contract(snippet: str) -> subprocess.CompletedProcess:
@@ -170,13 +170,19 @@ def _run_contract(snippet: str) -> subprocess.CompletedProcess:
         ("i8 upload bounds", "K.upload_i8_rows(0, 16, 32, 4, 3, 2, 16)"),
         ("gather without ranks", _GATHER + "v.ranks = 0\nK.matmul_q4_gather(0, v, 0, 16, 16, 4096, 16, 16, 64)"),
         ("gather rank out of range", _GATHER + "v.rank = 2\nK.matmul_q4_gather(0, v, 0, 16, 16, 4096, 16, 16, 64)"),
-        ("gather null peer output", _GATHER + "v.y[1] = None\nK.matmul_q4_gather(0, v, 0, 16, 16, 4096, 16, 16, 64)"),
+        ("gather null peer tags", _GATHER + "v.tags[1] = None\nK.matmul_q4_gather(0, v, 0, 16, 16, 4096, 16, 16, 64)"),
+        ("gather null output", _GATHER + "v.y = None\nK.matmul_q4_gather(0, v, 0, 16, 16, 4096, 16, 16, 64)"),
+        ("gather batch 2 for the GEMV", _GATHER + "v.batch = 2\nK.matmul_q4_gather(0, v, 0, 16, 16, 4096, 16, 16, 64)"),
+        ("gather x outside wait_for", _GATHER + "K.matmul_q4_gather(0, v, 0, 16, 1 << 16, 4096, 16, 16, 64, "
+                                                "wait_for=v)"),
+        ("gather rows batch mismatch", _GATHER + "K.gather_rows(0, v, 0, 16, 16, 2)"),
         ("gather wait on a bad exchange", _GATHER + "w = K.GatherView()\n"
                                           "K.matmul_q4_gather(0, v, 0, 16, 16, 4096, 16, 16, 64, wait_for=w)"),
         ("gather negative first row", _GATHER + "K.matmul_q4_gather(0, v, -16, 16, 16, 4096, 16, 16, 64)"),
         ("gather rows past the buffer", _GATHER + "K.matmul_q4_gather(0, v, 56, 16, 16, 4096, 16, 16, 64)"),
         ("gather without a row count", _GATHER + "v.rows = 0\nK.matmul_q4_gather(0, v, 0, 16, 16, 4096, 16, 16, 64)"),
         ("gather wait without ranks", _GATHER + "v.ranks = 0\nK.gather_wait(0, v)"),
+        ("gather wait without a batch", _GATHER + "v.batch = 0\nK.gather_wait(0, v)"),
     ],
 )
 def test_contract_violations_abort(case, call):

@@ -2,13 +2,14 @@
 
 The reference's consumers split output rows over devices and gather the
 slices with kunlun::peer copies (src/k200.cpp:89-95, docs/common-q4.md:31);
-here each rank's GEMV stores its rows into every rank's output buffer and
-publishes an epoch.  Checks:
+here each rank's GEMV stores its rows as tagged words {f32, epoch} into
+every rank's tag array of the exchange.  Checks:
   * ranks run one after another on one GPU (every wait is already satisfied
-    when it starts, so no kernel waits on one that has not run): every rank's
-    buffer holds every shard, bit-identical to k200_matmul on that shard, and
-    a chained second GEMV that waits for the first exchange reads the full
-    vector; flags carry one epoch per exchange use;
+    when it starts, so no kernel waits on one that has not run): after
+    k200_gather_wait every rank's buffer holds every shard, bit-identical to
+    k200_matmul on that shard, and a chained second GEMV that reads the first
+    exchange's tagged words sees the full vector; every word carries the
+    exchange's epoch, one per use;
   * a wait that nothing satisfies runs out and posts the peer-timeout status
     (0x4b03) instead of hanging, and the device stays usable;
   * on two GPUs (when present), the same chain across two processes.
@@ -57,18 +58,28 @@ def _download(K, ptr, n):
     return out
 
 
-def _flags(K, ex, world):
-    out = np.empty(world, np.uint32)
+def _epoch(K, view):
+    """This rank's current epoch of an exchange (its counter's second word)."""
+    out = np.empty(2, np.uint32)
     K.select(0)
-    K.check(K.copy(out, ex.view(0).flags[ex.rank], out.nbytes, K.DEVICE_TO_HOST))
-    return out
+    K.check(K.copy(out, view.counter, out.nbytes, K.DEVICE_TO_HOST))
+    return int(out[1])
 
 
-@pytest.mark.parametrize("world", [2, 3])
-def test_gather_ranks_on_one_gpu(K, O, gpu, world):
-    # the second GEMV reads 2048 values of the gathered 2000-row output: its
-    # rows plus the zeroed padding of the 2048-float buffer
-    k1, n1 = 4096, 2000
+def _tag_epochs(K, view, count):
+    """The epochs carried by the first `count` words of this rank's tag array."""
+    out = np.empty(count, np.uint64)
+    K.select(0)
+    K.check(K.copy(out, view.tags[view.rank], out.nbytes, K.DEVICE_TO_HOST))
+    return (out >> np.uint64(32)).astype(np.uint32)
+
+
+@pytest.mark.parametrize("world,n1", [(2, 2000), (3, 2000), (2, 2001)])
+def test_gather_ranks_on_one_gpu(K, O, gpu, world, n1):
+    # the second GEMV reads 2048 values of the gathered 2000- (2001-) row
+    # output: its tagged rows, then the zeroed padding of the 2048-float
+    # buffer read plainly (2001: a block whose first 17 values are tagged)
+    k1 = 4096
     k2, n2 = 2048, 1024
     q_up = _q4(O, k1, n1, 0x7340D123)
     q_dn = _q4(O, k2, n2, 0x1234567)
@@ -96,6 +107,9 @@ def test_gather_ranks_on_one_gpu(K, O, gpu, world):
             # x of the second GEMV: the first 2048 rows of this rank's gathered up output
             assert K.matmul_q4_gather(0, dn[r].view(step), b, dw2.data() + b * rb2, up[r].output(step), k2, c,
                                       sbuf.data(), scratch, wait_for=up[r].view(step)) == 0
+        for r in range(world):
+            assert K.gather_wait(0, up[r].view(step)) == 0
+            assert K.gather_wait(0, dn[r].view(step)) == 0
         K.select(0)
         assert K.wait() == 0
         full_up = np.concatenate([_plain(K, dw1, dx.data(), k1, row_shard(n1, world, r)[1], row_shard(n1, world, r)[0])
@@ -103,8 +117,10 @@ def test_gather_ranks_on_one_gpu(K, O, gpu, world):
         for r in range(world):
             got = _download(K, up[r].output(step), n1)
             assert np.array_equal(got.view(np.uint32), full_up.view(np.uint32)), f"rank {r} up rows"
-            assert (_flags(K, up[r], world) == step + 1).all()
-            assert (_flags(K, dn[r], world) == step + 1).all()
+            # exchange `step` is used once here (buffer 0, then buffer 1): epoch 1 each
+            assert _epoch(K, up[r].view(step)) == 1 and _epoch(K, dn[r].view(step)) == 1
+            assert (_tag_epochs(K, up[r].view(step), n1) == 1).all()
+            assert (_tag_epochs(K, dn[r].view(step), n2) == 1).all()
         xin = up[0].output(step)
         full_dn = np.concatenate([_plain(K, dw2, xin, k2, row_shard(n2, world, r)[1], row_shard(n2, world, r)[0])
                                   for r in range(world)])
@@ -117,11 +133,11 @@ def test_gather_ranks_on_one_gpu(K, O, gpu, world):
 
 
 def test_gather_wait_runs_out(K, gpu):
-    """A flag that no rank sets: the device-side wait gives up with the peer-timeout status."""
+    """Words that no rank stores: the device-side wait gives up with the peer-timeout status."""
     ex = PeerExchange.on_one_device(K, 0, 64, 2)
-    own = np.array([1], np.uint32)  # rank 0 claims epoch 1; rank 1 never publishes it
+    own = np.array([0, 1], np.uint32)  # rank 0 claims epoch 1; nobody stores words of epoch 1
     K.select(0)
-    K.check(K.copy(ex[0].view(0).flags[0], own, 4, K.HOST_TO_DEVICE))
+    K.check(K.copy(ex[0].view(0).counter, own, 8, K.HOST_TO_DEVICE))
     assert K.gather_wait(0, ex[0].view(0)) == 0
     K.select(0)
     assert K.wait() == PEER_TIMEOUT
@@ -187,6 +203,8 @@ def test_gather_rows_uneven_on_one_gpu(K, O, gpu, wtype, k, n, batch, world):
         K.matmul(kern, 0, ys, dw.data() + b * row_bytes, dx, k, c, batch, t)
         assert K.gather_rows(0, ex[r].view(0), b, ys, c, batch) == 0
         shards.append(ys)
+    for r in range(world):
+        assert K.gather_wait(0, ex[r].view(0)) == 0
     K.select(0)
     assert K.wait() == 0
     whole = np.empty((batch, n), np.float32)
@@ -199,7 +217,7 @@ def test_gather_rows_uneven_on_one_gpu(K, O, gpu, wtype, k, n, batch, world):
     for r in range(world):
         got = _download(K, ex[r].output(0), n * batch)
         assert np.array_equal(got.view(np.uint32), whole.view(np.uint32)), f"rank {r}"
-        assert (_flags(K, ex[r], world) == 1).all()
+        assert _epoch(K, ex[r].view(0)) == 1 and (_tag_epochs(K, ex[r].view(0), n * batch) == 1).all()
     assert (np.abs(whole - gold) <= bar * (1 + np.abs(gold))).all()
     kern.close()
     for e in reversed(ex):

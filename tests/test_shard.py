@@ -133,8 +133,8 @@ def _ranks_over_gloo(rank, world, port, out):
 
     ex = PeerExchange.over_group(K, 0, 1000, world, rank, all_gather)
     v0, v1 = ex.view(0), ex.view(1)
-    out.put((rank, [v0.y[r] for r in range(world)], [v1.y[r] for r in range(world)],
-             [v0.flags[r] for r in range(world)], v0.counter, ex.output(1), list(K.opened)))
+    out.put((rank, [v0.tags[r] for r in range(world)], [v1.tags[r] for r in range(world)], v0.y, v1.y,
+             v0.counter, v1.counter, ex.output(1), (v0.rows, v0.batch), list(K.opened)))
     ex.close()
     assert sorted(K.closed) == sorted(K.opened)
     dist.destroy_process_group()
@@ -157,13 +157,15 @@ def test_peer_exchange_views_over_gloo():
     for p in procs:
         p.join(60)
         assert p.exitcode == 0
-    pad = PeerExchange.padded(1000) * 4
-    assert pad == 1024 * 4
-    for rank, y0, y1, flags, counter, out1, opened in res:
+    pad = PeerExchange.padded(1000)
+    assert pad == 1024
+    assert PeerExchange.region_bytes(1000) == 2 * (pad * 12 + 64)
+    for rank, t0, t1, y0, y1, c0, c1, out1, shape, opened in res:
         for r in range(world):
             base = 0x10000 * (r + 1) + (0 if r == rank else 0x1000000)
-            assert y0[r] == base and y1[r] == base + pad
-            assert flags[r] == base + 2 * pad
+            assert t0[r] == base + 2 * pad * 4 and t1[r] == base + 2 * pad * 4 + pad * 8
         own = 0x10000 * (rank + 1)
-        assert counter == own + 2 * pad + 64 and out1 == own + pad
+        assert y0 == own and y1 == own + pad * 4 and out1 == y1
+        assert c0 == own + 2 * pad * 12 and c1 == c0 + 64
+        assert shape == (1000, 1)
         assert len(opened) == world - 1
