@@ -900,20 +900,46 @@ __global__ void __launch_bounds__(kThreadsQ4, 1) gemm_q4_kernel(const __grid_con
 
 // Activation rows for the f16 kernel: x[b, :] = 2^e[b] * (hi + lo), e chosen so that the
 // row's largest magnitude lies in [2^14, 2^15) (f16 hi/lo keep ~22 bits for
-// values down to ~2^-28 of it).  One CTA per row.
-// (permute: K positions in the q4_pos order of each 32-element block).
-__global__ void __launch_bounds__(256) split_rows_kernel(const float *x, int k, int x_stride, __half *hi, __half *lo,
-                                                         float *scale, int permute) {
-    __shared__ uint32_t red[8];
-    const float *src = x + static_cast<long long>(blockIdx.x) * x_stride;
+// values down to ~2^-28 of it).  One CTA per row and one thread per 32-element
+// block of it (K <= 16384: at most 512 threads): the row is read once into
+// registers (eight 16-byte loads a thread when vec4), its largest magnitude
+// reduced over the CTA, and each block's hi and lo halves leave as four
+// 16-byte stores each.  kPermute: K positions in the q4_pos order of each
+// 32-element block (the Q4_0 kernel's operand order).
+template <bool kPermute>
+__global__ void __launch_bounds__(512) split_rows_kernel(const float *x, int k, int x_stride, __half *hi, __half *lo,
+                                                         float *scale, int vec4) {
+    pdl_launch_dependents();  // the GEMM may start streaming its weights
+    pdl_wait_prior();         // x may be the previous kernel's output
+    __shared__ uint32_t red[16];
+    const int blk = threadIdx.x;
+    const bool active = blk < (k >> 5);
+    const float *src = x + static_cast<long long>(blockIdx.x) * x_stride + 32 * blk;
+    float v[32];
     uint32_t m = 0;
-    for (int j = threadIdx.x; j < k; j += blockDim.x) m = max(m, __float_as_uint(src[j]) & 0x7fffffffu);
+    if (active) {
+        if (vec4) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const float4 f = __ldg(reinterpret_cast<const float4 *>(src) + q);
+                v[4 * q] = f.x;
+                v[4 * q + 1] = f.y;
+                v[4 * q + 2] = f.z;
+                v[4 * q + 3] = f.w;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __ldg(src + i);
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) m = max(m, __float_as_uint(v[i]) & 0x7fffffffu);
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
     __syncthreads();
     m = 0;
-    for (int i = 0; i < (blockDim.x >> 5); ++i) m = max(m, red[i]);
+    for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) m = max(m, red[i]);
     int e = 0;
     if (m != 0 && m < 0x7f800000u) {
         int ex = static_cast<int>(m >> 23) - 127;
@@ -921,14 +947,26 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const float *x, int k, 
         e = min(max(ex - 14, -126), 113);
     }
     const float s = __uint_as_float(static_cast<uint32_t>(127 - e) << 23);
-    __half *h = hi + static_cast<long long>(blockIdx.x) * k, *l = lo + static_cast<long long>(blockIdx.x) * k;
-    for (int j = threadIdx.x; j < k; j += blockDim.x) {
-        const float v = __fmul_rn(src[j], s);
-        const __half hv = __float2half_rn(v);
-        const float hf = __half2float(hv);
-        const int p = permute ? (j & ~31) + q4_pos(j & 31) : j;
-        h[p] = hv;
-        l[p] = (__float_as_uint(hf) & 0x7fffffffu) < 0x7f800000u ? __float2half_rn(__fsub_rn(v, hf)) : __ushort_as_half(0);
+    if (active) {
+        uint32_t hw[16] = {}, lw[16] = {};  // f16 bits, two per word, in (permuted) K order
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const float u = __fmul_rn(v[i], s);
+            const __half h = __float2half_rn(u);
+            const float hf = __half2float(h);
+            const __half l = (__float_as_uint(hf) & 0x7fffffffu) < 0x7f800000u ? __float2half_rn(__fsub_rn(u, hf))
+                                                                               : __ushort_as_half(0);
+            const int p = kPermute ? q4_pos(i) : i;
+            hw[p >> 1] |= static_cast<uint32_t>(__half_as_ushort(h)) << (16 * (p & 1));
+            lw[p >> 1] |= static_cast<uint32_t>(__half_as_ushort(l)) << (16 * (p & 1));
+        }
+        const long long off = static_cast<long long>(blockIdx.x) * k + 32 * blk;
+        uint4 *ho = reinterpret_cast<uint4 *>(hi + off), *lo4 = reinterpret_cast<uint4 *>(lo + off);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            ho[q] = make_uint4(hw[4 * q], hw[4 * q + 1], hw[4 * q + 2], hw[4 * q + 3]);
+            lo4[q] = make_uint4(lw[4 * q], lw[4 * q + 1], lw[4 * q + 2], lw[4 * q + 3]);
+        }
     }
     if (threadIdx.x == 0) scale[blockIdx.x] = __uint_as_float(static_cast<uint32_t>(e + 127) << 23);
 }
@@ -1111,8 +1149,18 @@ cudaError_t launch_gemm_tc(const GemvRequest &r, const DeviceInfo &dev, cudaStre
         char *sbase = static_cast<char *>(r.split);
         __half *hi = reinterpret_cast<__half *>(sbase), *lo = reinterpret_cast<__half *>(sbase + part);
         float *sc = reinterpret_cast<float *>(sbase + 2 * part);
-        split_rows_kernel<<<r.batch, 256, 0, stream>>>(r.x, r.k, r.x_stride, hi, lo, sc, q4 ? 1 : 0);
-        cudaError_t e = cudaGetLastError();
+        const int vec4 = (reinterpret_cast<uintptr_t>(r.x) & 15) == 0 && r.x_stride % 4 == 0;
+        cudaLaunchConfig_t scfg{};
+        scfg.gridDim = dim3(r.batch);
+        scfg.blockDim = dim3((r.k / 32 + 31) / 32 * 32);
+        scfg.stream = stream;
+        cudaLaunchAttribute sattr[1];
+        sattr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        sattr[0].val.programmaticStreamSerializationAllowed = 1;
+        scfg.attrs = sattr;
+        scfg.numAttrs = 1;
+        cudaError_t e = cudaLaunchKernelEx(&scfg, q4 ? split_rows_kernel<true> : split_rows_kernel<false>, r.x, r.k,
+                                           r.x_stride, hi, lo, sc, vec4);
         if (e != cudaSuccess) return e;
         b0 = hi;
         b1 = lo;
