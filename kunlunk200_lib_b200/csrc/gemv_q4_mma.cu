@@ -47,10 +47,14 @@
 //    and adds them to its own partial sums of that tile in shared memory when
 //    the tile changes; after the last box the CTA's warps meet at
 //    one barrier and finish the CTA's tiles (one warp per tile): sum the
-//    warps' partials in warp order and store Y, or, for a tile shared with
-//    other CTAs, publish the sum (if a lower CTA holds the tile's first
-//    units) or collect the higher CTAs' published sums in CTA order before
-//    storing Y, so results do not depend on timing.
+//    warps' partials in warp order and store Y.  A tile shared with other
+//    CTAs is finished by the CTA that holds its first units, which adds the
+//    higher CTAs' sums in CTA order, so results do not depend on timing.
+//    Those sums move early: every consumer warp signals when it is past its
+//    first row tile, and the producer warp (idle once its boxes are issued)
+//    then publishes the CTA's sum of that tile and collects the higher CTAs'
+//    sums of the CTA's last tile into shared memory while the consumers are
+//    still working, so the finish does not wait on another CTA's loop.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -85,6 +89,9 @@ constexpr int kWarps = K200_Q4_GEMV_WARPS;             // consumer warps, four p
 constexpr int kQuads = kWarps / 4;                     // box j is read by quad j mod kQuads
 constexpr int kStages = 16;                            // ring stages (box j in stage j mod 16)
 constexpr int kThreads = (kWarps + 1) * 32;
+// A row tile has at most 64 units (K <= 16384) and every CTA at least one, so
+// at most 63 later CTAs share a CTA's last tile.
+constexpr int kMaxPeers = 64;
 static_assert(kWarps % 4 == 0 && kWarps >= 16, "consumer warps come in quads, at least one per four stages");
 
 struct Q4MmaArgs {
@@ -365,9 +372,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t *ring = smem;
     uint8_t *xrec = ring + kStages * kStageBytes;
     float *part = reinterpret_cast<float *>(xrec + groups * kRecBytes);  // [max_tiles][kWarps][16]
-    uint64_t *full = reinterpret_cast<uint64_t *>(part + a.max_tiles * kWarps * kTileRows);
+    float *peer = part + a.max_tiles * kWarps * kTileRows;  // [kMaxPeers][16]: later CTAs' sums of the last tile
+    uint64_t *full = reinterpret_cast<uint64_t *>(peer + kMaxPeers * kTileRows);
     uint64_t *empty = full + kStages;
-    volatile uint32_t *box_tab = reinterpret_cast<volatile uint32_t *>(empty + kStages);  // [max_boxes]
+    uint64_t *first_done = empty + kStages;  // every consumer lane is past the first row tile
+    uint64_t *peers_in = first_done + 1;     // the producer warp has collected the last tile's peer sums
+    volatile uint32_t *box_tab = reinterpret_cast<volatile uint32_t *>(peers_in + 1);  // [max_boxes]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int u0 = static_cast<int>(blockIdx.x * a.units / static_cast<uint32_t>(a.grid));
@@ -378,13 +388,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (tid < kStages) {
         mbar_init(&full[tid], 1);
         mbar_init(&empty[tid], kMaxBoxPairs);  // one arrival per unit slot of a box
+        if (tid == 0) {
+            mbar_init(first_done, kWarps * 32);
+            mbar_init(peers_in, 32);
+        }
         fence_mbar_init();
     }
     __syncthreads();
     pdl_launch_dependents();
 
+    // Row tiles shared with other CTAs: this CTA's first tile began in a lower
+    // CTA (which finishes it) when p_first > 0; its last tile continues in
+    // higher CTAs (whose sums this CTA collects) when collect_last.
+    const int p_first = u0 - t_first * a.ppr;
+    const int p_end = u1 - t_last * a.ppr;
+    const bool collect_last = (t_last + 1) * a.ppr > static_cast<int>(u1) && t_last * a.ppr >= static_cast<int>(u0);
+
     if (warp == kWarps) {
         // ---------------- producer ----------------
+        int issued = 0;
         if (lane == 0) {
 #pragma unroll
             for (int m = 0; m < kMaxBoxPairs; ++m)
@@ -408,8 +430,48 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (bw.width < kMaxBoxPairs) mbar_arrive_count(&empty[s], kMaxBoxPairs - bw.width);
             }
             if (j <= early) pdl_wait_prior();
+            issued = j;
+        }
+        __syncwarp();
+        pdl_wait_prior();  // the partial-sum words were cleared by the previous launch's collectors
+        // Publish the sum of the first row tile as soon as the consumers are
+        // past it (the lower CTA that finishes the tile then finds it early),
+        // and collect the higher CTAs' sums of the last row tile while the
+        // consumers still work, so neither waits at the end.
+        if (p_first > 0) {
+            bool ok = false;
+            for (uint32_t i = 0; i < kWaitBudget && !ok; ++i) ok = mbar_try_wait(first_done, 0);
+            if (!ok) atomicExch(a.err, kErrBulkTimeout);
+            if (lane < kTileRows) {
+                float v = 0.f;
+#pragma unroll
+                for (int w = 0; w < kWarps; ++w) v += part[w * kTileRows + lane];
+                st_relaxed(a.slot + static_cast<size_t>(blockIdx.x) * kTileRows + lane, kPresent | __float_as_uint(v));
+            }
+        }
+        if (collect_last) {
+            const int last = cta_of(static_cast<uint32_t>((t_last + 1) * a.ppr - 1), a.units, a.grid);
+            if (lane < kTileRows) {
+                for (int j0 = blockIdx.x + 1; j0 <= last; ++j0) {
+                    unsigned long long *src = a.slot + static_cast<size_t>(j0) * kTileRows + lane;
+                    unsigned long long w = ld_relaxed(src);
+                    for (uint32_t spin = 0; !(w & kPresent); ++spin) {
+                        if (spin >= kPeerBudget) {
+                            atomicExch(a.err, kErrPeerTimeout);
+                            break;
+                        }
+                        __nanosleep(64);
+                        w = ld_relaxed(src);
+                    }
+                    peer[(j0 - blockIdx.x - 1) * kTileRows + lane] = __uint_as_float(static_cast<uint32_t>(w));
+                    st_relaxed(src, 0ull);
+                }
+            }
+            mbar_arrive(peers_in);
+        }
+        if (lane == 0) {
             // never exit with a copy still writing into this CTA's shared memory
-            for (int i = j > kStages ? j - kStages : 0; i < j; ++i)
+            for (int i = issued > kStages ? issued - kStages : 0; i < issued; ++i)
                 (void)mbar_wait_sleep(&full[i % kStages], (i / kStages) & 1, a.err, kErrBulkTimeout, 128);
         }
         return;
@@ -516,34 +578,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int w = 0; w < kWarps; ++w) v += part[(ts * kWarps + w) * kTileRows + lane];
         const int tb = t * a.ppr, te = tb + a.ppr;
         const int row = t * kTileRows + lane;
-        if (tb < u0) {
-            st_relaxed(a.slot + static_cast<size_t>(blockIdx.x) * kTileRows + lane, kPresent | __float_as_uint(v));
-            return;
-        }
+        if (tb < u0) return;  // the producer warp published this CTA's sum of the tile
         if (te > u1) {
+            // the sums of the higher CTAs that hold the rest of the tile, in CTA order
+            bool ok = false;
+            for (uint32_t i = 0; i < kWaitBudget && !ok; ++i) ok = mbar_try_wait(peers_in, 0);
+            if (!ok) atomicExch(a.err, kErrPeerTimeout);
             const int last = cta_of(static_cast<uint32_t>(te - 1), a.units, a.grid);
-            for (int j0 = blockIdx.x + 1; j0 <= last; j0 += 4) {
-                unsigned long long wv[4];
-#pragma unroll
-                for (int q = 0; q < 4; ++q)
-                    wv[q] = j0 + q <= last ? ld_relaxed(a.slot + static_cast<size_t>(j0 + q) * kTileRows + lane)
-                                           : kPresent;
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    if (j0 + q > last) break;
-                    unsigned long long *src = a.slot + static_cast<size_t>(j0 + q) * kTileRows + lane;
-                    for (uint32_t spin = 0; !(wv[q] & kPresent); ++spin) {
-                        if (spin >= kPeerBudget) {
-                            atomicExch(a.err, kErrPeerTimeout);
-                            break;
-                        }
-                        __nanosleep(64);
-                        wv[q] = ld_relaxed(src);
-                    }
-                    v += __uint_as_float(static_cast<uint32_t>(wv[q]));
-                    st_relaxed(src, 0ull);
-                }
-            }
+            for (int q = 0; q < last - static_cast<int>(blockIdx.x); ++q) v += peer[q * kTileRows + lane];
         }
         if (row < a.n) {
             a.y[row] = v;
@@ -556,8 +598,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
 
     // boxes of this CTA: the first segment, the full row tiles, the last segment
-    const int p_first = u0 - t_first * a.ppr;
-    const int p_end = u1 - t_last * a.ppr;
     const int nboxes = t_first == t_last ? boxes_in(p_end - p_first)
                                          : boxes_in(a.ppr - p_first) + (t_last - t_first - 1) * boxes_in(a.ppr) +
                                                boxes_in(p_end);
@@ -569,6 +609,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quad_r = warp >> 2, slot_q = warp & 3;  // quad of the warp, its unit slot in a box
     float acc0 = 0.f, acc1 = 0.f;  // rows g and g + 8 of the current row tile
     int cur = -1;
+    bool past_first = false;  // arrived on first_done
     auto flush = [&](int t) {
         acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
         acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
@@ -587,6 +628,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&full[s], (j / kStages) & 1, a.err, kErrBulkTimeout)) break;
         const uint32_t info = box_tab[j];
         const int width = static_cast<int>(info >> 24);
+        if (!past_first && (info & 0xffffu) != 0) {
+            // this warp is done with the first row tile: its sums go to shared
+            // memory now, for the producer warp's early publish
+            if (cur == 0) {
+                flush(0);
+                cur = -1;
+            }
+            past_first = true;
+            mbar_arrive(first_done);
+        }
         if (slot_q < width) {
             const int tile_l = static_cast<int>(info & 0xffffu), pair = static_cast<int>((info >> 16) & 0xffu) + slot_q;
             if (tile_l != cur) {
@@ -640,6 +691,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
     if (cur >= 0) flush(cur);
+    if (!past_first) mbar_arrive(first_done);
     consumer_sync();  // every warp's partials are in shared memory
     for (int ts = warp; ts <= t_last - t_first; ts += kWarps) finish_tile(ts);
     if (kGather && xg.ranks > 0) {
@@ -680,7 +732,8 @@ bool q4_mma_plan(Q4MmaPlan &p, int k, int n, const DeviceInfo &dev) {
     p.max_boxes = static_cast<int>(per / kMaxBoxPairs + p.max_tiles + 1);  // >= the boxes of any range
     if (p.tiles >= (1 << 16)) return false;                                 // box table: 16-bit tile index
     p.smem = static_cast<size_t>(kStages) * kStageBytes + static_cast<size_t>(k / 128) * kRecBytes +
-             sizeof(float) * p.max_tiles * kWarps * kTileRows + 16 * kStages + 4 * static_cast<size_t>(p.max_boxes);
+             sizeof(float) * (p.max_tiles * kWarps + kMaxPeers) * kTileRows + 16 * kStages + 16 +
+             4 * static_cast<size_t>(p.max_boxes);
     return p.smem + 1024 <= static_cast<size_t>(dev.smem_optin);
 }
 
