@@ -270,38 +270,54 @@ __device__ __forceinline__ void load_slot(const float *xb, int p, int c, float (
 // The same eight activations when X is another exchange's output: tagged
 // words {f32, epoch} (exchange.cuh) for the block's first `lim` elements,
 // plain floats after them (the zeroed padding past the exchange's rows).
-// issue_slot_tagged starts the 16-byte loads of the tagged element pairs;
-// resolve_slot_tagged waits for words that do not carry `epoch` yet and
-// returns the values in load_slot's order.
+// issue_slot_tagged starts the loads of the tagged words.
 __device__ __forceinline__ void issue_slot_tagged(const unsigned long long *tb, int lim, int p, int c,
                                                   unsigned long long (&w)[8]) {
     const int a0 = pair_first(p, c), a1 = pair_second(p, c);
     const int e[4] = {a0, a1, a0 + 16, a1 + 16};
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-        if (e[q] + 1 < lim) {
-            ld_tag2(tb + e[q], w[2 * q], w[2 * q + 1]);
-        } else {
-            w[2 * q] = 0ull;
-            w[2 * q + 1] = 0ull;
-        }
+        w[2 * q] = 0ull;
+        w[2 * q + 1] = 0ull;
+        if (e[q] + 1 < lim) ld_tag2(tb + e[q], w[2 * q], w[2 * q + 1]);
+        else if (e[q] < lim) w[2 * q] = ld_tag(tb + e[q]);
     }
 }
-__device__ __forceinline__ void resolve_slot_tagged(const unsigned long long *tb, const float *xb, int lim, int p,
-                                                    int c, const unsigned long long (&w)[8], unsigned epoch,
-                                                    int *err, float (&v)[8]) {
+// One round of the wait for a slot's tagged words: re-issues the loads of
+// the words that do not carry `epoch` yet and returns whether there were any
+// (their new values are checked in the next round, so the rounds of all of a
+// thread's slots share one round trip).
+__device__ __forceinline__ bool refresh_slot_tagged(const unsigned long long *tb, int lim, int p, int c,
+                                                    unsigned long long (&w)[8], unsigned epoch) {
+    const int a0 = pair_first(p, c), a1 = pair_second(p, c);
+    const int e[4] = {a0, a1, a0 + 16, a1 + 16};
+    bool any = false;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const bool stale = (e[q] < lim && tag_epoch(w[2 * q]) != epoch) ||
+                           (e[q] + 1 < lim && tag_epoch(w[2 * q + 1]) != epoch);
+        if (!stale) continue;
+        any = true;
+        if (e[q] + 1 < lim) ld_tag2(tb + e[q], w[2 * q], w[2 * q + 1]);
+        else w[2 * q] = ld_tag(tb + e[q]);
+    }
+    return any;
+}
+// The slot's eight activations once its words are current, in load_slot's order.
+__device__ __forceinline__ void values_slot_tagged(const float *xb, int lim, int p, int c,
+                                                   const unsigned long long (&w)[8], float (&v)[8]) {
     const int a0 = pair_first(p, c), a1 = pair_second(p, c);
     const int e[4] = {a0, a1, a0 + 16, a1 + 16};
     float2 f[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
         if (e[q] + 1 < lim) {
-            f[q].x = await_tag(tb + e[q], w[2 * q], epoch, err);
-            f[q].y = await_tag(tb + e[q] + 1, w[2 * q + 1], epoch, err);
+            f[q].x = tag_value(w[2 * q]);
+            f[q].y = tag_value(w[2 * q + 1]);
         } else if (e[q] >= lim) {
             f[q] = __ldcg(reinterpret_cast<const float2 *>(xb + e[q]));
         } else {  // the last tagged element, then padding
-            f[q].x = await_tag(tb + e[q], ld_tag(tb + e[q]), epoch, err);
+            f[q].x = tag_value(w[2 * q]);
             f[q].y = __ldcg(xb + e[q] + 1);
         }
     }
@@ -514,14 +530,33 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int b = ((pr < a.ppr ? pr : pr - a.ppr) * 32 + (t & 31)) >> 2;
                     issue_slot_tagged(xg.wait_tags + 32 * b, xg.wait_tagged - 32 * b, b & 3, lane & 3, xw[k]);
                 }
+            // every pass's stale words are re-loaded together: one round trip per round
+            for (uint32_t spin = 0;; ++spin) {
+                bool any = false;
+#pragma unroll
+                for (int k = 0; k < kPasses; ++k)
+                    if (k * kWarps * 32 < count) {
+                        const int t = min(k * kWarps * 32 + tid, count - 1);
+                        const int pr = p_start + (t >> 5);
+                        const int b = ((pr < a.ppr ? pr : pr - a.ppr) * 32 + (t & 31)) >> 2;
+                        any |= refresh_slot_tagged(xg.wait_tags + 32 * b, xg.wait_tagged - 32 * b, b & 3, lane & 3,
+                                                   xw[k], wait_epoch);
+                    }
+                if (!any) break;
+                if (spin >= kTagBudget ||
+                    ((spin & 255u) == 255u && *reinterpret_cast<volatile int *>(a.err) == kErrPeerTimeout)) {
+                    atomicExch(a.err, kErrPeerTimeout);
+                    break;
+                }
+                __nanosleep(64);
+            }
 #pragma unroll
             for (int k = 0; k < kPasses; ++k)
                 if (k * kWarps * 32 < count) {
                     const int t = min(k * kWarps * 32 + tid, count - 1);
                     const int pr = p_start + (t >> 5);
                     const int b = ((pr < a.ppr ? pr : pr - a.ppr) * 32 + (t & 31)) >> 2;
-                    resolve_slot_tagged(xg.wait_tags + 32 * b, a.x + 32 * b, xg.wait_tagged - 32 * b, b & 3,
-                                        lane & 3, xw[k], wait_epoch, a.err, xv[k]);
+                    values_slot_tagged(a.x + 32 * b, xg.wait_tagged - 32 * b, b & 3, lane & 3, xw[k], xv[k]);
                 }
         } else {
 #pragma unroll
