@@ -16,9 +16,14 @@
 //
 // Layout and work split:
 //  * the unit of work is 16 rows x 144 bytes of the weight matrix (eight
-//    Q4_0 blocks of each row, two "groups" of four blocks).  Units are
-//    numbered row-tile-major and every CTA (one per SM) takes a contiguous
-//    range of them, so the bytes per CTA are balanced to within one unit;
+//    Q4_0 blocks of each row, two "groups" of four blocks).  K is cut into
+//    parts of at most 16 units (4096 values; one part up to K = 4096), the
+//    CTAs (one per SM) are shared out to the parts in proportion to their
+//    units, and within a part the units are numbered row-tile-major and
+//    every CTA takes a contiguous range of them, so the bytes per CTA are
+//    balanced to within about one unit and a CTA prepares at most 16 KiB of
+//    X.  The last part's CTA that finishes a row tile adds the other parts'
+//    sums of it in part order;
 //  * a producer thread streams the CTA's range as "boxes" of 16 rows x 1-4
 //    units (2-D TMA tensor copies, cp.async.bulk.tensor + mbarriers): each
 //    row tile's part of the range is cut into boxes of four units (576-byte
@@ -58,6 +63,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
@@ -89,18 +95,26 @@ constexpr int kWarps = K200_Q4_GEMV_WARPS;             // consumer warps, four p
 constexpr int kQuads = kWarps / 4;                     // box j is read by quad j mod kQuads
 constexpr int kStages = 16;                            // ring stages (box j in stage j mod 16)
 constexpr int kThreads = (kWarps + 1) * 32;
-// A row tile has at most 64 units (K <= 16384) and every CTA at least one, so
-// at most 63 later CTAs share a CTA's last tile.
-constexpr int kMaxPeers = 64;
+// K is cut into at most kMaxParts parts of at most kPartPairs pairs (256
+// values): a CTA works on one part, so it reads and converts at most 16 KiB of
+// X, and a row tile of a part has at most 16 units, so at most 15 later CTAs
+// share a CTA's last tile.
+constexpr int kPartPairs = 16;
+constexpr int kMaxParts = 4;
+constexpr int kMaxPeers = kPartPairs;
 static_assert(kWarps % 4 == 0 && kWarps >= 16, "consumer warps come in quads, at least one per four stages");
 
 struct Q4MmaArgs {
     const float *x;
     float *y;
     unsigned long long *slot;  // [grid][16] tagged partial sums of row tiles shared with other CTAs
+    unsigned long long *vt;    // [tiles][parts - 1][16] tagged sums of a row tile over K parts 0 .. parts-2
     int *err;
-    uint32_t units;     // row tiles * units per row (units * (grid + 1) < 2^32: 32-bit index math)
-    int k, n, tiles, ppr, grid, prefetch;
+    int k, n, tiles, grid, prefetch;
+    int parts;                       // K parts (units of part s: row tiles x pairs [part_pair[s], part_pair[s+1]))
+    int part_pair[kMaxParts + 1];    // first pair of each part (and ppr at the end)
+    int part_cta[kMaxParts + 1];     // first CTA of each part (and grid at the end), in proportion to its units
+    int rec_groups;                  // activation records held (2 x the pairs of the largest part)
     int max_tiles;      // row tiles any CTA touches (partial-sum slots in shared memory)
     int max_boxes;      // boxes any CTA streams (entries of the box table)
 };
@@ -384,10 +398,9 @@ template <bool kGather>
 __global__ void __launch_bounds__(kThreads, 1)
     q4_mma_gemv_kernel(const __grid_constant__ Q4MmaMaps maps, const Q4MmaArgs a, const __grid_constant__ GatherLaunch xg) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const int groups = a.k >> 7;
     uint8_t *ring = smem;
-    uint8_t *xrec = ring + kStages * kStageBytes;
-    float *part = reinterpret_cast<float *>(xrec + groups * kRecBytes);  // [max_tiles][kWarps][16]
+    uint8_t *xrec = ring + kStages * kStageBytes;  // [rec_groups] records, by group within the K part
+    float *part = reinterpret_cast<float *>(xrec + a.rec_groups * kRecBytes);  // [max_tiles][kWarps][16]
     float *peer = part + a.max_tiles * kWarps * kTileRows;  // [kMaxPeers][16]: later CTAs' sums of the last tile
     uint64_t *full = reinterpret_cast<uint64_t *>(peer + kMaxPeers * kTileRows);
     uint64_t *empty = full + kStages;
@@ -396,10 +409,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile uint32_t *box_tab = reinterpret_cast<volatile uint32_t *>(peers_in + 1);  // [max_boxes]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int u0 = static_cast<int>(blockIdx.x * a.units / static_cast<uint32_t>(a.grid));
-    const int u1 = static_cast<int>((blockIdx.x + 1) * a.units / static_cast<uint32_t>(a.grid));
-    const int t_first = u0 / a.ppr;
-    const int t_last = (u1 - 1) / a.ppr;
+    // This CTA's K part: CTAs cta0 .. cta0 + grid_p - 1 share its units, the
+    // row tiles x its pairs [pair0, pair0 + ppr), numbered row-tile-major;
+    // CTA `cta` of the part takes a contiguous, balanced range of them.
+    int part_s = 0, cta0 = a.part_cta[0], cta_end = a.part_cta[1], pair0 = a.part_pair[0], pair_end = a.part_pair[1];
+#pragma unroll
+    for (int s = 1; s < kMaxParts; ++s)  // constant indices: the parameter arrays stay in the constant bank
+        if (s < a.parts && static_cast<int>(blockIdx.x) >= a.part_cta[s]) {
+            part_s = s;
+            cta0 = a.part_cta[s];
+            cta_end = a.part_cta[s + 1];
+            pair0 = a.part_pair[s];
+            pair_end = a.part_pair[s + 1];
+        }
+    const int grid_p = cta_end - cta0, cta = static_cast<int>(blockIdx.x) - cta0, ppr = pair_end - pair0;
+    const uint32_t units = static_cast<uint32_t>(a.tiles) * static_cast<uint32_t>(ppr);
+    const int u0 = static_cast<int>(static_cast<uint32_t>(cta) * units / static_cast<uint32_t>(grid_p));
+    const int u1 = static_cast<int>(static_cast<uint32_t>(cta + 1) * units / static_cast<uint32_t>(grid_p));
+    const int t_first = u0 / ppr;
+    const int t_last = (u1 - 1) / ppr;
 
     if (tid < kStages) {
         mbar_init(&full[tid], 1);
@@ -416,9 +444,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Row tiles shared with other CTAs: this CTA's first tile began in a lower
     // CTA (which finishes it) when p_first > 0; its last tile continues in
     // higher CTAs (whose sums this CTA collects) when collect_last.
-    const int p_first = u0 - t_first * a.ppr;
-    const int p_end = u1 - t_last * a.ppr;
-    const bool collect_last = (t_last + 1) * a.ppr > static_cast<int>(u1) && t_last * a.ppr >= static_cast<int>(u0);
+    const int p_first = u0 - t_first * ppr;
+    const int p_end = u1 - t_last * ppr;
+    const bool collect_last = (t_last + 1) * ppr > u1 && t_last * ppr >= u0;
 
     if (warp == kWarps) {
         // ---------------- producer ----------------
@@ -431,7 +459,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int early = a.prefetch < kStages ? a.prefetch : kStages;
             const uint32_t ring_u = smem_u32(ring);
             int j = 0;
-            for (BoxWalk bw(u0, u1, a.ppr); bw.u < u1 && j < a.max_boxes; bw.next(), ++j) {
+            for (BoxWalk bw(u0, u1, ppr); bw.u < u1 && j < a.max_boxes; bw.next(), ++j) {
                 const int s = j % kStages;
                 if (j >= kStages && !mbar_wait_sleep(&empty[s], ((j / kStages) & 1) ^ 1, a.err, kErrBulkTimeout, 128))
                     break;
@@ -440,7 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 box_tab[j] = static_cast<uint32_t>(bw.tile - t_first) | (static_cast<uint32_t>(bw.pair) << 16) |
                              (static_cast<uint32_t>(bw.width) << 24);
                 mbar_arrive_expect_tx(&full[s], kTileRows * 4 * box_words(bw.width));
-                tma_load_2d(ring_u + s * kStageBytes, &maps.box[bw.width - 1], bw.pair * kPairWords,
+                tma_load_2d(ring_u + s * kStageBytes, &maps.box[bw.width - 1], (pair0 + bw.pair) * kPairWords,
                             bw.tile * kTileRows, &full[s], policy);
                 // the unit slots a narrow box lacks are released here
                 if (bw.width < kMaxBoxPairs) mbar_arrive_count(&empty[s], kMaxBoxPairs - bw.width);
@@ -466,10 +494,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
         if (collect_last) {
-            const int last = cta_of(static_cast<uint32_t>((t_last + 1) * a.ppr - 1), a.units, a.grid);
+            const int last = cta_of(static_cast<uint32_t>((t_last + 1) * ppr - 1), units, grid_p);
             if (lane < kTileRows) {
-                for (int j0 = blockIdx.x + 1; j0 <= last; ++j0) {
-                    unsigned long long *src = a.slot + static_cast<size_t>(j0) * kTileRows + lane;
+                for (int j0 = cta + 1; j0 <= last; ++j0) {
+                    unsigned long long *src = a.slot + static_cast<size_t>(cta0 + j0) * kTileRows + lane;
                     unsigned long long w = ld_relaxed(src);
                     for (uint32_t spin = 0; !(w & kPresent); ++spin) {
                         if (spin >= kPeerBudget) {
@@ -479,7 +507,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         __nanosleep(64);
                         w = ld_relaxed(src);
                     }
-                    peer[(j0 - blockIdx.x - 1) * kTileRows + lane] = __uint_as_float(static_cast<uint32_t>(w));
+                    peer[(j0 - cta - 1) * kTileRows + lane] = __uint_as_float(static_cast<uint32_t>(w));
                     st_relaxed(src, 0ull);
                 }
             }
@@ -503,19 +531,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     {
         // fragment records: four threads per activation block; every load of a
         // thread is issued before the first conversion.  Only the unit pairs
-        // (256-element K ranges, 32 slots each) that this CTA's units touch
-        // are built: the pairs p_first .. ppr-1 and 0 .. p_end-1 of its first
-        // and last row tiles, i.e. every pair once the range covers a whole
-        // row tile.  (K <= 16384: at most 2048 slots.)
-        constexpr int kPasses = (2048 + kWarps * 32 - 1) / (kWarps * 32);
-        const int pf = u0 - t_first * a.ppr, pe = u1 - t_last * a.ppr;
-        int p_start = 0, npairs = a.ppr;
+        // (256-element K ranges, 32 slots each) of the CTA's K part that its
+        // units touch are built: the pairs p_first .. ppr-1 and 0 .. p_end-1
+        // of its first and last row tiles, i.e. every pair of the part once
+        // the range covers a whole row tile.  (At most kPartPairs pairs.)
+        constexpr int kPasses = (kPartPairs * 32 + kWarps * 32 - 1) / (kWarps * 32);
+        const int pf = u0 - t_first * ppr, pe = u1 - t_last * ppr;
+        int p_start = 0, npairs = ppr;
         if (t_first == t_last) {
             p_start = pf;
             npairs = pe - pf;
         } else if (t_last == t_first + 1 && pe <= pf) {
             p_start = pf;
-            npairs = a.ppr - pf + pe;
+            npairs = ppr - pf + pe;
         }
         const int count = 32 * npairs;  // a multiple of 32: whole warps are inside or past the range
         float xv[kPasses][8];
@@ -527,7 +555,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (k * kWarps * 32 < count) {
                     const int t = min(k * kWarps * 32 + tid, count - 1);
                     const int pr = p_start + (t >> 5);
-                    const int b = ((pr < a.ppr ? pr : pr - a.ppr) * 32 + (t & 31)) >> 2;
+                    const int b = (((pr < ppr ? pr : pr - ppr) * 32 + (t & 31)) >> 2) + 8 * pair0;
                     issue_slot_tagged(xg.wait_tags + 32 * b, xg.wait_tagged - 32 * b, b & 3, lane & 3, xw[k]);
                 }
             // every pass's stale words are re-loaded together: one round trip per round
@@ -538,7 +566,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (k * kWarps * 32 < count) {
                         const int t = min(k * kWarps * 32 + tid, count - 1);
                         const int pr = p_start + (t >> 5);
-                        const int b = ((pr < a.ppr ? pr : pr - a.ppr) * 32 + (t & 31)) >> 2;
+                        const int b = (((pr < ppr ? pr : pr - ppr) * 32 + (t & 31)) >> 2) + 8 * pair0;
                         any |= refresh_slot_tagged(xg.wait_tags + 32 * b, xg.wait_tagged - 32 * b, b & 3, lane & 3,
                                                    xw[k], wait_epoch);
                     }
@@ -555,7 +583,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (k * kWarps * 32 < count) {
                     const int t = min(k * kWarps * 32 + tid, count - 1);
                     const int pr = p_start + (t >> 5);
-                    const int b = ((pr < a.ppr ? pr : pr - a.ppr) * 32 + (t & 31)) >> 2;
+                    const int b = (((pr < ppr ? pr : pr - ppr) * 32 + (t & 31)) >> 2) + 8 * pair0;
                     values_slot_tagged(a.x + 32 * b, xg.wait_tagged - 32 * b, b & 3, lane & 3, xw[k], xv[k]);
                 }
         } else {
@@ -564,7 +592,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (k * kWarps * 32 < count) {
                     const int t = min(k * kWarps * 32 + tid, count - 1);
                     const int pr = p_start + (t >> 5);
-                    const int b = ((pr < a.ppr ? pr : pr - a.ppr) * 32 + (t & 31)) >> 2;
+                    const int b = (((pr < ppr ? pr : pr - ppr) * 32 + (t & 31)) >> 2) + 8 * pair0;
                     load_slot(a.x + 32 * b, b & 3, lane & 3, xv[k]);
                 }
         }
@@ -573,8 +601,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (k * kWarps * 32 < count) {
                 const int t0 = k * kWarps * 32 + tid, t = min(t0, count - 1);
                 const int pr = p_start + (t >> 5);
-                const int b = ((pr < a.ppr ? pr : pr - a.ppr) * 32 + (t & 31)) >> 2;
-                store_slot(xv[k], xrec + (b >> 2) * kRecBytes, b & 3, lane & 3, t0 < count);
+                const int br = ((pr < ppr ? pr : pr - ppr) * 32 + (t & 31)) >> 2;  // block within the part
+                store_slot(xv[k], xrec + (br >> 2) * kRecBytes, br & 3, lane & 3, t0 < count);
             }
     }
     for (int i = tid; i < a.max_tiles * kWarps * kTileRows; i += kWarps * 32) part[i] = 0.f;
@@ -611,7 +639,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         float v = 0.f;
 #pragma unroll
         for (int w = 0; w < kWarps; ++w) v += part[(ts * kWarps + w) * kTileRows + lane];
-        const int tb = t * a.ppr, te = tb + a.ppr;
+        const int tb = t * ppr, te = tb + ppr;
         const int row = t * kTileRows + lane;
         if (tb < u0) return;  // the producer warp published this CTA's sum of the tile
         if (te > u1) {
@@ -619,8 +647,33 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = false;
             for (uint32_t i = 0; i < kWaitBudget && !ok; ++i) ok = mbar_try_wait(peers_in, 0);
             if (!ok) atomicExch(a.err, kErrPeerTimeout);
-            const int last = cta_of(static_cast<uint32_t>(te - 1), a.units, a.grid);
-            for (int q = 0; q < last - static_cast<int>(blockIdx.x); ++q) v += peer[q * kTileRows + lane];
+            const int last = cta_of(static_cast<uint32_t>(te - 1), units, grid_p);
+            for (int q = 0; q < last - cta; ++q) v += peer[q * kTileRows + lane];
+        }
+        if (a.parts > 1) {
+            // the row tile's sum over K parts: parts 0 .. parts-2 publish theirs,
+            // the last part's finishing CTA adds them in part order, then its own
+            unsigned long long *vt = a.vt + static_cast<size_t>(t) * (a.parts - 1) * kTileRows + lane;
+            if (part_s + 1 < a.parts) {
+                st_relaxed(vt + part_s * kTileRows, kPresent | __float_as_uint(v));
+                return;
+            }
+            float sum = 0.f;
+            for (int q = 0; q + 1 < a.parts; ++q) {
+                unsigned long long w = ld_relaxed(vt + q * kTileRows);
+                for (uint32_t spin = 0; !(w & kPresent); ++spin) {
+                    if (spin >= kPeerBudget) {
+                        atomicExch(a.err, kErrPeerTimeout);
+                        break;
+                    }
+                    __nanosleep(64);
+                    w = ld_relaxed(vt + q * kTileRows);
+                }
+                const float f = __uint_as_float(static_cast<uint32_t>(w));
+                sum = q == 0 ? f : sum + f;
+                st_relaxed(vt + q * kTileRows, 0ull);
+            }
+            v = sum + v;
         }
         if (row < a.n) {
             a.y[row] = v;
@@ -634,7 +687,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // boxes of this CTA: the first segment, the full row tiles, the last segment
     const int nboxes = t_first == t_last ? boxes_in(p_end - p_first)
-                                         : boxes_in(a.ppr - p_first) + (t_last - t_first - 1) * boxes_in(a.ppr) +
+                                         : boxes_in(ppr - p_first) + (t_last - t_first - 1) * boxes_in(ppr) +
                                                boxes_in(p_end);
     const uint32_t ring_u = smem_u32(ring), xrec_u = smem_u32(xrec);
     // Warp 4r + q takes unit slot q of boxes r, r + Q, r + 2Q, ... (Q quads):
@@ -750,7 +803,8 @@ __global__ void __launch_bounds__(256) gather_wait_kernel(const unsigned long lo
 }
 
 struct Q4MmaPlan {
-    int grid, tiles, ppr, max_tiles, max_boxes;
+    int grid, tiles, ppr, parts, max_tiles, max_boxes, rec_groups;
+    int part_pair[kMaxParts + 1], part_cta[kMaxParts + 1];
     long long units;
     size_t smem;
 };
@@ -762,11 +816,37 @@ bool q4_mma_plan(Q4MmaPlan &p, int k, int n, const DeviceInfo &dev) {
     p.units = static_cast<long long>(p.tiles) * p.ppr;
     p.grid = static_cast<int>(p.units < dev.sm_count ? p.units : dev.sm_count);
     if (p.units * (p.grid + 1) >= (1ll << 32)) return false;  // the kernel's index math is 32-bit
-    const long long per = (p.units + p.grid - 1) / p.grid;
-    p.max_tiles = static_cast<int>((per + p.ppr - 1) / p.ppr + 1);
+    if (p.tiles >= (1 << 16)) return false;                    // box table: 16-bit tile index
+    // K parts of at most kPartPairs pairs, their boundaries on multiples of
+    // four pairs where that keeps every part within kPartPairs (a row tile's
+    // part is then streamed as full 4-unit boxes, but for the last one), and
+    // CTAs in proportion to the parts' units
+    p.parts = (p.ppr + kPartPairs - 1) / kPartPairs;
+    if (p.parts > kMaxParts) return false;
+    bool aligned = true;
+    for (int s = 0; s <= p.parts; ++s) {
+        p.part_pair[s] = s == p.parts ? p.ppr : (2 * s * p.ppr + 4 * p.parts) / (8 * p.parts) * 4;
+        if (s > 0 && (p.part_pair[s] - p.part_pair[s - 1] < 1 || p.part_pair[s] - p.part_pair[s - 1] > kPartPairs))
+            aligned = false;
+    }
+    for (int s = 0; s <= p.parts; ++s) {
+        if (!aligned) p.part_pair[s] = s * p.ppr / p.parts;
+        p.part_cta[s] = static_cast<int>(static_cast<long long>(p.grid) * p.part_pair[s] / p.ppr);
+    }
+    long long per = 0;  // units of the largest CTA range
+    int min_ppr = p.ppr, max_ppr = 0;
+    for (int s = 0; s < p.parts; ++s) {
+        const int g = p.part_cta[s + 1] - p.part_cta[s], pp = p.part_pair[s + 1] - p.part_pair[s];
+        if (g < 1 || pp < 1) return false;
+        const long long u = static_cast<long long>(p.tiles) * pp;
+        per = std::max(per, (u + g - 1) / g);
+        min_ppr = std::min(min_ppr, pp);
+        max_ppr = std::max(max_ppr, pp);
+    }
+    p.max_tiles = static_cast<int>((per + min_ppr - 1) / min_ppr + 1);
     p.max_boxes = static_cast<int>(per / kMaxBoxPairs + p.max_tiles + 1);  // >= the boxes of any range
-    if (p.tiles >= (1 << 16)) return false;                                 // box table: 16-bit tile index
-    p.smem = static_cast<size_t>(kStages) * kStageBytes + static_cast<size_t>(k / 128) * kRecBytes +
+    p.rec_groups = 2 * max_ppr;
+    p.smem = static_cast<size_t>(kStages) * kStageBytes + static_cast<size_t>(p.rec_groups) * kRecBytes +
              sizeof(float) * (p.max_tiles * kWarps + kMaxPeers) * kTileRows + 16 * kStages + 16 +
              4 * static_cast<size_t>(p.max_boxes);
     return p.smem + 1024 <= static_cast<size_t>(dev.smem_optin);
@@ -835,7 +915,9 @@ bool weight_maps(Q4MmaMaps &out, const void *w, int k, int n) {
 size_t q4_mma_scratch_bytes(int k, int n, int batch, const DeviceInfo &dev) {
     Q4MmaPlan p;
     if (batch != 1 || !q4_mma_plan(p, k, n, dev)) return 0;
-    return static_cast<size_t>(p.grid) * kTileRows * sizeof(unsigned long long);
+    // per CTA the sums of a shared row tile, per row tile the sums of K parts 0 .. parts-2
+    return (static_cast<size_t>(p.grid) + static_cast<size_t>(p.tiles) * (p.parts - 1)) * kTileRows *
+           sizeof(unsigned long long);
 }
 
 cudaError_t launch_q4_mma_gemv(const GemvRequest &r, const DeviceInfo &dev, cudaStream_t stream) {
@@ -850,13 +932,18 @@ cudaError_t launch_q4_mma_gemv(const GemvRequest &r, const DeviceInfo &dev, cuda
     a.x = r.x;
     a.y = r.y;
     a.slot = static_cast<unsigned long long *>(r.fixup);
+    a.vt = a.slot + static_cast<size_t>(p.grid) * kTileRows;
     a.err = dev.err;
-    a.units = static_cast<uint32_t>(p.units);
     a.k = r.k;
     a.n = r.n;
     a.tiles = p.tiles;
-    a.ppr = p.ppr;
     a.grid = p.grid;
+    a.parts = p.parts;
+    for (int s = 0; s <= kMaxParts; ++s) {
+        a.part_pair[s] = s <= p.parts ? p.part_pair[s] : p.ppr;
+        a.part_cta[s] = s <= p.parts ? p.part_cta[s] : p.grid;
+    }
+    a.rec_groups = p.rec_groups;
     a.prefetch = r.prefetch_weights ? 1 << 30 : 0;
     a.max_tiles = p.max_tiles;
     a.max_boxes = p.max_boxes;

@@ -74,13 +74,14 @@ def _tag_epochs(K, view, count):
     return (out >> np.uint64(32)).astype(np.uint32)
 
 
-@pytest.mark.parametrize("world,n1", [(2, 2000), (3, 2000), (2, 2001)])
-def test_gather_ranks_on_one_gpu(K, O, gpu, world, n1):
-    # the second GEMV reads 2048 values of the gathered 2000- (2001-) row
-    # output: its tagged rows, then the zeroed padding of the 2048-float
-    # buffer read plainly (2001: a block whose first 17 values are tagged)
+@pytest.mark.parametrize("world,n1,k2", [(2, 2000, 2048), (3, 2000, 2048), (2, 2001, 2048), (2, 5100, 5120)])
+def test_gather_ranks_on_one_gpu(K, O, gpu, world, n1, k2):
+    # the second GEMV reads k2 values of the gathered n1-row output: its
+    # tagged rows, then the zeroed padding of the exchange buffer read plainly
+    # (2001: a block whose first 17 values are tagged; 5100 of 5120: K cut
+    # into two parts of 12 and 8 pairs, the second ending in padding)
     k1 = 4096
-    k2, n2 = 2048, 1024
+    n2 = 1024
     q_up = _q4(O, k1, n1, 0x7340D123)
     q_dn = _q4(O, k2, n2, 0x1234567)
     x = O.uniform(0x09200ABC, k1, -1.0, 1.0)
