@@ -837,8 +837,8 @@ bool q4_mma_plan(Q4MmaPlan &p, int k, int n, const DeviceInfo &dev) {
     int min_ppr = p.ppr, max_ppr = 0;
     for (int s = 0; s < p.parts; ++s) {
         const int g = p.part_cta[s + 1] - p.part_cta[s], pp = p.part_pair[s + 1] - p.part_pair[s];
-        if (g < 1 || pp < 1) return false;
         const long long u = static_cast<long long>(p.tiles) * pp;
+        if (g < 1 || pp < 1 || g > u) return false;  // every CTA holds at least one unit
         per = std::max(per, (u + g - 1) / g);
         min_ppr = std::min(min_ppr, pp);
         max_ppr = std::max(max_ppr, pp);

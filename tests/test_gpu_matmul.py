@@ -109,6 +109,14 @@ def _q4_case(O, k, n, batch, seed=0x7340D123):
         (3072, 4100, 1),
         (4608, 1234, 1),
         (16384, 5000, 1),
+        # K parts of the batch-1 GEMV (at most 16 units each, boundaries on
+        # multiples of four where they fit): 33 units -> 12 + 12 + 9, 48 ->
+        # 16 x 3, 61 -> proportional 15 + 15 + 15 + 16, and 64 units over
+        # three row tiles, each tile split over a dozen CTAs of its part
+        (8448, 700, 1),
+        (12288, 2000, 1),
+        (15616, 300, 1),
+        (16384, 48, 1),
     ],
 )
 def test_q4_0_matches_fp64_gold(K, O, gpu, k, n, batch):
