@@ -12,8 +12,9 @@
 //
 // Epochs: every rank keeps a private {arrivals, epoch} counter per exchange.
 // A launch that stores into the exchange tags its words with epoch + 1 (read
-// after the previous kernel of its stream completed); its blocks count
-// themselves in and the last one raises the counter's epoch.  Every rank
+// after the previous kernel of its stream completed); each block counts itself
+// in as soon as all of its threads have read the epoch, and the last one
+// raises the counter's epoch (only kernels after this launch read it).  Every rank
 // issues the same sequence of launches per exchange, so the ranks' epochs
 // agree.  A reader expects its own rank's current epoch of the exchange.
 // Tag arrays start zeroed (epoch 0: nothing published yet).
@@ -76,10 +77,11 @@ __device__ __forceinline__ float await_tag(const unsigned long long *p, unsigned
     return tag_value(w);
 }
 
-// End of a launch that stored words of `epoch`, by one thread of every block
-// after the block's barrier: the last block to arrive resets the arrivals and
-// raises the exchange's epoch for the launches that follow on this stream
-// (which read it only after this launch has completed).
+// A block of a launch that stores words of `epoch` counts itself in (one
+// thread, after a barrier behind every thread's read of the epoch): the last
+// block to arrive resets the arrivals and raises the exchange's epoch for the
+// launches that follow on this stream (which read it only after this launch
+// has completed).
 __device__ __forceinline__ void count_launch(unsigned *counter, int blocks, unsigned epoch) {
     if (atomicAdd(counter, 1u) + 1u == static_cast<unsigned>(blocks)) {
         counter[0] = 0u;

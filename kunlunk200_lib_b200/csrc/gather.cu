@@ -25,11 +25,15 @@ namespace {
 
 // Grid-stride pass over the [batch][n] slice, two columns at a time (one
 // 16-byte store of two tagged words per rank) when the offsets allow it,
-// then the launch is counted in.
+// after the launch is counted in.
 __global__ void __launch_bounds__(256) gather_rows_kernel(float *y, const float *shard, int n, int batch, int rows,
                                                           const __grid_constant__ GatherLaunch xg, int vec2) {
     pdl_wait_prior();  // the counter and the tags' previous contents belong to earlier kernels
     const unsigned epoch = exchange_epoch(xg.counter) + 1u;
+    // every thread has read the epoch: the block counts in before its stores
+    // (the last one raises the epoch, which only kernels after this launch read)
+    __syncthreads();
+    if (threadIdx.x == 0) count_launch(xg.counter, gridDim.x, epoch);
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
     const long long first = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
     if (vec2) {
@@ -55,8 +59,6 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(float *y, const float 
             for (int r = 0; r < xg.ranks; ++r) st_tag(xg.tags[r] + b * rows + j, w);
         }
     }
-    __syncthreads();  // every thread has read the epoch before the block counts in
-    if (threadIdx.x == 0) count_launch(xg.counter, gridDim.x, epoch);
 }
 
 }  // namespace

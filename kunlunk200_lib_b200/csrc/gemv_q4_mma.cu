@@ -607,6 +607,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = tid; i < a.max_tiles * kWarps * kTileRows; i += kWarps * 32) part[i] = 0.f;
     consumer_sync();
+    // every consumer thread has read this launch's epoch: count the block in
+    // now (the last one raises the exchange's epoch, which only kernels after
+    // this launch read), so the count's round trip is not on the launch's tail
+    if (kGather && xg.ranks > 0 && tid == 0) count_launch(xg.counter, a.grid, epoch);
 
     const int g = lane >> 2, c = lane & 3;
     // The five words lane c loads from each of its rows, as byte offsets in
@@ -782,12 +786,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!past_first) mbar_arrive(first_done);
     consumer_sync();  // every warp's partials are in shared memory
     for (int ts = warp; ts <= t_last - t_first; ts += kWarps) finish_tile(ts);
-    if (kGather && xg.ranks > 0) {
-        // every consumer thread has read the epoch: count the block in (the
-        // last one raises the exchange's epoch for the launches that follow)
-        consumer_sync();
-        if (tid == 0) count_launch(xg.counter, a.grid, epoch);
-    }
 }
 
 // The end of a sharded sequence (launch_gather_wait): waits for the first
