@@ -733,20 +733,51 @@ def measure_gemm(K, torch, dist, dev: int, stream, world: int, rank: int, wname:
         else:
             x = torch.rand((batch, k), generator=gen, device="cuda", dtype=torch.float32) * 2 - 1
         y_sh = torch.empty((batch, n_sh), device="cuda")
-        y_full = y_sh if world == 1 else torch.empty((world, batch, n_sh), device="cuda")
+    # N > 1: Y is gathered over NVLink.  Outputs up to 8 MB take the library's
+    # row gather (k200_gather_rows: every rank's slice as tagged words into every
+    # rank's exchange, no collective, then k200_gather_wait writes the full
+    # [batch][n] Y on the device) -- a few microseconds where NCCL's all-gather
+    # costs ~10-15; larger ones take NCCL's all-gather, whose plain 4-byte
+    # values cross NVLink once instead of as 8-byte tagged words.
+    peer = world > 1 and batch * n * 4 <= (8 << 20)
+    y_full = y_sh if world == 1 or peer else torch.empty((world, batch, n_sh), device="cuda")
     stream.synchronize()
     kern = K.Kernel()
     i8 = wname == "rowwise_i8"
+    ex = None
+    if peer:
+        from kunlunk200_lib_b200.shard import PeerExchange
+
+        def all_gather_obj(obj):
+            got = [None] * world
+            dist.all_gather_object(got, obj)
+            return got
+
+        ex = PeerExchange.over_group(K, dev, n, world, rank, all_gather_obj, batch=batch)
+        row_begin = row_shard(n, world, rank)[0]
+        dist.barrier()  # every rank's regions are mapped before any rank stores into them
+        torch.cuda.synchronize()
 
     def step(s_: int):
         W = weights[s_ % sets]
         sc = K.packed_i8_scales(W, k, n_sh) if i8 else None
         mx = K.packed_i8_maxima(W, k, n_sh) if i8 else None
         K.matmul(kern, dev, y_sh, W, x, k, n_sh, batch, wtype, sc, mx)
-        if world > 1:
+        if peer:
+            # steps alternate between two exchange buffers (every sequence of
+            # steps below has an even length, so the alternation never breaks)
+            K.check(K.gather_rows(dev, ex.view(s_), row_begin, y_sh, n_sh, batch))
+            K.check(K.gather_wait(dev, ex.view(s_)))
+        elif world > 1:
             dist.all_gather_into_tensor(y_full, y_sh)
 
+    def y_out(s_: int) -> int:
+        """Address of step s_'s gathered Y on this rank."""
+        return ex.output(s_) if peer else y_full.data_ptr()
+
     nwarm = max(3, warmup)
+    if world > 1:
+        nwarm += nwarm % 2
     w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         step(0)  # first call: scratch growth, kernel set-up
@@ -763,6 +794,9 @@ def measure_gemm(K, torch, dist, dev: int, stream, world: int, rank: int, wname:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         steps = int(min(4000, max(20, target_s / max(float(t.item()), 1e-6))))
     per_graph = sets * max(1, 24 // sets)
+    if world > 1:  # even sequences of steps: the exchange buffers alternate by step parity
+        steps += steps % 2
+        per_graph *= 1 + per_graph % 2
     reps, rem = divmod(steps, per_graph)
 
     def capture(nsteps: int):
@@ -821,7 +855,7 @@ def measure_gemm(K, torch, dist, dev: int, stream, world: int, rank: int, wname:
     # passes) and the matmul kernel itself
     tc = batch >= 4 and k % 16 == 0 and (wname != "q4_0" or k % 256 == 0) and wname != "f32"
     prep = (1 if (tc and wname in ("q4_0", "f16")) else 0) + ((1 if batch * k <= 65536 else 3) if i8 else 0)
-    launches = steps * (1 + prep)
+    launches = steps * (1 + prep + (2 if peer else 0))
     peaks = read_peaks()
     hbm_gbs = shard_bytes / (ms_step * 1e-3) / 1e9
     tflops_gpu = flops_step / world / (ms_step * 1e-3) / 1e12
@@ -844,7 +878,7 @@ def measure_gemm(K, torch, dist, dev: int, stream, world: int, rank: int, wname:
     e2e_steps = max(10, min(steps, 500))
     xh = torch.empty((batch, k), dtype=torch.float32).pin_memory()
     xh.copy_(x.cpu())
-    yh = torch.empty(y_full.numel(), dtype=torch.float32).pin_memory()
+    yh = torch.empty(batch * n, dtype=torch.float32).pin_memory()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -854,7 +888,7 @@ def measure_gemm(K, torch, dist, dev: int, stream, world: int, rank: int, wname:
         for i in range(e2e_steps):
             K.check(K.copy_async(x, xh, xh.numel() * 4, K.HOST_TO_DEVICE))
             step(i)
-            K.check(K.copy_async(yh, y_full, yh.numel() * 4, K.DEVICE_TO_HOST))
+            K.check(K.copy_async(yh, y_out(i), yh.numel() * 4, K.DEVICE_TO_HOST))
             K.check(K.wait())
         e1.record(stream)
     stream.synchronize()
@@ -867,6 +901,9 @@ def measure_gemm(K, torch, dist, dev: int, stream, world: int, rank: int, wname:
         v, cores, kind, sample = gemm_cpu_rate(wname, k, n, batch, cpu_seconds)
         cpu = {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": kind, "sample": sample}
     del g_main, g_rem
+    if ex is not None:
+        dist.barrier()  # no rank still reads another's region
+        ex.close()
     kern.close()
     del weights
     torch.cuda.synchronize()
@@ -878,7 +915,8 @@ def measure_gemm(K, torch, dist, dev: int, stream, world: int, rank: int, wname:
         "steps": steps, "warmup": warmup, "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": gemm_dtype(wname), "data": "synthetic",
         "config": {"workload": f"{wname} matmul K{k} N{n} batch {batch} ({label})", "k": k, "n": n, "batch": batch,
-                   "parallelism": f"row-shard{world}+allgather" if world > 1 else "single",
+                   "parallelism": (f"row-shard{world}+" + ("peer-gather" if peer else "nccl-allgather")) if world > 1
+                                  else "single",
                    "work": "logical 2*N*K*batch per step",
                    "l2": f"{sets} rotating weight sets ({sets * shard_bytes / 1e6:.0f} MB per GPU)",
                    "timing": "CUDA graph replays, CUDA events on the launching stream, max over ranks"},
